@@ -1,0 +1,162 @@
+"""Headline benchmark: Qwen3-30B-A3B-shaped full SFT step, tokens/s for the whole job.
+
+Config: 48 layers, hidden 2048, 32 q / 4 kv heads, head_dim 128, RoPE theta
+1e6, 128 experts top-8 with intermediate 768, vocab 151936; seq 4096, batch 1 per rank,
+uniform-random token ids (synthetic), loss on the last 50% of tokens, random-init (std 0.02),
+AdamW with fp32 master weights, gradient checkpointing, EP = N (+ FSDP = N for dense weights).
+
+    python bench.py --gpus N --steps K --warmup W                 # native arm
+    python bench.py --impl reference --gpus N --steps K --warmup W  # unmodified reference arm
+
+For N > 1 launch with ``python -m torch.distributed.run --nproc-per-node N ... bench.py``.
+Rank 0 prints one JSON line. The device-timed ``value`` brackets exactly K steps with a barrier
+and ``torch.cuda.synchronize()`` on both sides and takes the max over ranks; the ``e2e`` value
+times the same steps through the public training API including the pinned host-to-device copy of
+each step's tokens and the device-to-host read of its loss.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "SFT tokens/sec/box (max over ranks)"
+MODEL = "Qwen3-30B-A3B-shaped (48L, H2048, 32q/4kv x128, 128 experts top-8, I768, V151936)"
+# The reference publishes no B200 or Qwen number; the only published SFT throughput is DSV4-Flash
+# on 8x B300, which is a different model, so vs_baseline stays null.
+BASELINE_VALUE = None
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser(description=__doc__)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=5)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=("native", "reference"), default="native")
+    p.add_argument("--seq-len", type=int, default=4096)
+    p.add_argument("--batch-size", type=int, default=1)
+    p.add_argument("--layers", type=int, default=48, help="development only: fewer layers is not the benchmark")
+    p.add_argument("--dispatcher", choices=("auto", "nccl", "nvlink"), default="auto")
+    p.add_argument("--moment-dtype", choices=("fp32", "bf16"), default="fp32")
+    p.add_argument("--lr", type=float, default=1e-5)
+    return p.parse_args(argv)
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.samples: list[list[str]] = []
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self) -> None:
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                for line in out.stdout.strip().splitlines():
+                    self.samples.append([x.strip() for x in line.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        self._thread.join(timeout=10)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit())
+        mx = max((float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()), default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 5 + i and s[5 + i] == "Active"})
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(self.samples)}
+
+
+def emit(record: dict) -> None:
+    print(json.dumps(record), flush=True)
+
+
+def memory_plan(args, world: int) -> tuple[bool, str]:
+    """Whether the full optimizer state fits in HBM at this N (fp32 master + moments per rank)."""
+    from tiny_dsv41_b200.models.qwen import Qwen3MoeConfig
+
+    cfg = Qwen3MoeConfig(num_hidden_layers=args.layers)
+    experts = cfg.num_hidden_layers * cfg.num_experts * 3 * cfg.hidden_size * cfg.moe_intermediate_size
+    dense = (cfg.num_hidden_layers * (cfg.hidden_size * (cfg.num_attention_heads + 2 * cfg.num_key_value_heads)
+                                      * cfg.head_dim * 2 + cfg.hidden_size * cfg.num_experts)
+             + 2 * cfg.vocab_size * cfg.hidden_size)
+    per_rank = experts / world + dense / world
+    moment_bytes = 8 if args.moment_dtype == "fp32" else 4
+    bytes_per_param = 2 + 2 + 4 + moment_bytes  # bf16 param + bf16 grad + fp32 master + moments
+    need = per_rank * bytes_per_param
+    budget = 160e9
+    return need <= budget, (f"{(experts + dense) / 1e9:.1f}B params; {per_rank / 1e9:.2f}B per rank x "
+                            f"{bytes_per_param} B (bf16 param+grad, fp32 master, {args.moment_dtype} moments) "
+                            f"= {need / 1e9:.0f} GB > {budget / 1e9:.0f} GB of HBM per B200")
+
+
+def run_native(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from tiny_dsv41_b200.train.qwen_sft import QwenSFTBench
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    fits, why = memory_plan(args, world)
+    base = {"metric": METRIC, "impl": "native", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic",
+            "unit": "tokens/s"}
+    if not fits:
+        if rank == 0:
+            emit({**base, "value": None, "unavailable": f"full config does not fit: {why}", "vs_baseline": None,
+                  "config": {"model": MODEL, "seq_len": args.seq_len, "global_batch": args.batch_size * world}})
+        return
+    bench = QwenSFTBench(args)
+    result = bench.run()
+    if rank == 0:
+        record = {**base, **result}
+        record["vs_baseline"] = (None if BASELINE_VALUE is None or record.get("value") is None
+                                 else record["value"] / BASELINE_VALUE)
+        emit(record)
+    bench.close()
+
+
+def run_reference(args) -> None:
+    sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+    from tiny_dsv41_b200.train.reference_arm import run_reference_arm
+
+    record = run_reference_arm(args, METRIC, MODEL)
+    if record is not None and int(os.environ.get("RANK", "0")) == 0:
+        emit(record)
+
+
+def main() -> None:
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_native(args)
+
+
+if __name__ == "__main__":
+    main()

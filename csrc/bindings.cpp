@@ -1,0 +1,87 @@
+// Python bindings of the sm_100a kernels (module tiny_dsv41_b200._C).
+#include <torch/extension.h>
+
+#include <vector>
+
+namespace tdsv {
+// status
+int64_t read_status();
+// norm.cu
+std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, double eps);
+std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
+                                    const at::Tensor& rstd, bool need_dw);
+at::Tensor column_sum(const at::Tensor& partial);
+// rope.cu
+std::vector<at::Tensor> qk_norm_rope_fwd(const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& wk,
+                                         const at::Tensor& pos, const at::Tensor& inv_freq, int64_t hq, int64_t hkv,
+                                         double eps);
+std::vector<at::Tensor> qk_norm_rope_bwd(const at::Tensor& dq, const at::Tensor& dk, const at::Tensor& dv,
+                                         const at::Tensor& qkv, const at::Tensor& wq, const at::Tensor& wk,
+                                         const at::Tensor& pos, const at::Tensor& inv_freq, int64_t hq, int64_t hkv,
+                                         double eps);
+at::Tensor rope_interleaved(const at::Tensor& x, const at::Tensor& pos, const at::Tensor& inv_freq, int64_t rope_dim,
+                            bool inverse);
+// router.cu
+std::vector<at::Tensor> router_fwd(const at::Tensor& logits, const c10::optional<at::Tensor>& bias, int64_t k,
+                                   int64_t func, bool normalize, double norm_eps, double scale);
+at::Tensor router_bwd(const at::Tensor& dweights, const at::Tensor& ids, const at::Tensor& scores,
+                      const at::Tensor& logits, const c10::optional<at::Tensor>& aux_coef, int64_t func,
+                      bool normalize, double norm_eps, double scale);
+// moe_permute.cu
+at::Tensor moe_gather(const at::Tensor& x, const at::Tensor& src);
+at::Tensor moe_combine(const at::Tensor& rows, const at::Tensor& idx, const c10::optional<at::Tensor>& w);
+std::vector<at::Tensor> moe_combine_bwd(const at::Tensor& dout, const at::Tensor& rows, const at::Tensor& idx,
+                                        const c10::optional<at::Tensor>& w, bool need_dw);
+void moe_zero_padding(at::Tensor& buf, const at::Tensor& src);
+// swiglu.cu
+at::Tensor swiglu_fwd(const at::Tensor& gu, const c10::optional<at::Tensor>& w, bool interleaved, double limit);
+std::vector<at::Tensor> swiglu_bwd(const at::Tensor& dout, const at::Tensor& gu, const c10::optional<at::Tensor>& w,
+                                   bool interleaved, double limit, bool need_dw);
+// loss.cu
+std::vector<at::Tensor> cross_entropy_fused(at::Tensor& logits, const at::Tensor& targets, double scale,
+                                            int64_t ignore_index, bool write_grad);
+std::vector<at::Tensor> token_logprob_fwd(const at::Tensor& logits, const at::Tensor& targets, double temperature);
+at::Tensor token_logprob_bwd(const at::Tensor& logits, const at::Tensor& targets, const at::Tensor& lse,
+                             const at::Tensor& dlogp, double temperature);
+// optim.cu
+void adamw_step(at::Tensor& master, const at::Tensor& grad, at::Tensor& m, at::Tensor& v,
+                const c10::optional<at::Tensor>& out, double lr, double beta1, double beta2, double eps,
+                double weight_decay, int64_t step, double grad_scale, const c10::optional<at::Tensor>& grad_scale_t);
+void sgd_step(at::Tensor& param, const at::Tensor& grad, const c10::optional<at::Tensor>& out, double lr,
+              double grad_scale, const c10::optional<at::Tensor>& nonfinite);
+at::Tensor grad_sq_norm(const at::Tensor& g);
+// gemm_tc.cu
+void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, bool b_mn, bool accumulate);
+void grouped_gemm_m(const at::Tensor& a, const at::Tensor& b, const at::Tensor& group_off,
+                    const at::Tensor& group_rows, at::Tensor& out, bool b_mn, int64_t max_rows);
+void grouped_gemm_k(const at::Tensor& a, const at::Tensor& b, const at::Tensor& group_off,
+                    const at::Tensor& group_rows, at::Tensor& out, bool accumulate);
+}  // namespace tdsv
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "tiny_dsv41_b200 sm_100a kernels";
+  m.def("read_status", &tdsv::read_status, "read and clear the device pipeline status word");
+  m.def("rmsnorm_fwd", &tdsv::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &tdsv::rmsnorm_bwd);
+  m.def("column_sum", &tdsv::column_sum);
+  m.def("qk_norm_rope_fwd", &tdsv::qk_norm_rope_fwd);
+  m.def("qk_norm_rope_bwd", &tdsv::qk_norm_rope_bwd);
+  m.def("rope_interleaved", &tdsv::rope_interleaved);
+  m.def("router_fwd", &tdsv::router_fwd);
+  m.def("router_bwd", &tdsv::router_bwd);
+  m.def("moe_gather", &tdsv::moe_gather);
+  m.def("moe_combine", &tdsv::moe_combine);
+  m.def("moe_combine_bwd", &tdsv::moe_combine_bwd);
+  m.def("moe_zero_padding", &tdsv::moe_zero_padding);
+  m.def("swiglu_fwd", &tdsv::swiglu_fwd);
+  m.def("swiglu_bwd", &tdsv::swiglu_bwd);
+  m.def("cross_entropy_fused", &tdsv::cross_entropy_fused);
+  m.def("token_logprob_fwd", &tdsv::token_logprob_fwd);
+  m.def("token_logprob_bwd", &tdsv::token_logprob_bwd);
+  m.def("adamw_step", &tdsv::adamw_step);
+  m.def("sgd_step", &tdsv::sgd_step);
+  m.def("grad_sq_norm", &tdsv::grad_sq_norm);
+  m.def("gemm", &tdsv::gemm);
+  m.def("grouped_gemm_m", &tdsv::grouped_gemm_m);
+  m.def("grouped_gemm_k", &tdsv::grouped_gemm_k);
+}

@@ -1,0 +1,165 @@
+// Fused optimizer updates over flat parameter buffers.
+//
+// adamw_step implements torch.optim.AdamW (decoupled weight decay, bias-corrected moments) on an
+// fp32 master buffer, reading fp32 or bf16 gradients, keeping the moments in fp32 or bf16, and
+// writing the bf16 compute copy of the parameters in the same pass. An optional device scalar
+// multiplies the gradient (global-norm clipping coefficient, 1/world, loss-scale undo) without a
+// host synchronisation.
+//
+// sgd_step implements the reference's SGD-in-backward update (dsv41_train/optim.py:13-82): plain
+// SGD on an fp32 master (or directly on the parameter), with a finite flag raised per launch.
+//
+// grad_sq_norm writes per-block partial sums of squares; the caller reduces them in fixed order.
+#include "common.cuh"
+
+namespace tdsv {
+
+namespace {
+
+template <typename GT, typename MT>
+__global__ void adamw_kernel(float* __restrict__ master, const GT* __restrict__ grad, MT* __restrict__ m,
+                             MT* __restrict__ v, __nv_bfloat16* __restrict__ out, int64_t n, float lr, float beta1,
+                             float beta2, float eps, float weight_decay, float bc1, float bc2_sqrt,
+                             float grad_scale, const float* __restrict__ grad_scale_ptr) {
+  const float gs = grad_scale * (grad_scale_ptr != nullptr ? *grad_scale_ptr : 1.f);
+  const float step_size = lr / bc1;
+  const float decay = 1.f - lr * weight_decay;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float g = to_float<GT>(grad[i]) * gs;
+    float p = master[i] * decay;
+    const float mi = beta1 * to_float<MT>(m[i]) + (1.f - beta1) * g;
+    const float vi = beta2 * to_float<MT>(v[i]) + (1.f - beta2) * g * g;
+    const float denom = sqrtf(vi) / bc2_sqrt + eps;
+    p -= step_size * mi / denom;
+    master[i] = p;
+    m[i] = from_float<MT>(mi);
+    v[i] = from_float<MT>(vi);
+    if (out != nullptr) out[i] = f2bf(p);
+  }
+}
+
+template <typename GT, typename PT>
+__global__ void sgd_kernel(PT* __restrict__ param, const GT* __restrict__ grad, __nv_bfloat16* __restrict__ out,
+                           int64_t n, float lr, float grad_scale, int* __restrict__ nonfinite) {
+  bool bad = false;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float g = to_float<GT>(grad[i]) * grad_scale;
+    bad |= !isfinite(g);
+    const float p = to_float<PT>(param[i]) - lr * g;
+    param[i] = from_float<PT>(p);
+    if (out != nullptr) out[i] = f2bf(p);
+  }
+  if (bad && nonfinite != nullptr) atomicExch(nonfinite, 1);
+}
+
+template <typename GT>
+__global__ void sq_norm_kernel(const GT* __restrict__ g, float* __restrict__ partial, int64_t n) {
+  __shared__ float scratch[32];
+  float s = 0.f;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float x = to_float<GT>(g[i]);
+    s += x * x;
+  }
+  s = block_sum(s, scratch);
+  if (threadIdx.x == 0) partial[blockIdx.x] = s;
+}
+
+int grid_for(int64_t n) {
+  const int64_t blocks = (n + 255) / 256;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(blocks, static_cast<int64_t>(num_sms()) * 8)));
+}
+
+}  // namespace
+
+void adamw_step(at::Tensor& master, const at::Tensor& grad, at::Tensor& m, at::Tensor& v,
+                const c10::optional<at::Tensor>& out, double lr, double beta1, double beta2, double eps,
+                double weight_decay, int64_t step, double grad_scale, const c10::optional<at::Tensor>& grad_scale_t) {
+  check_cuda_tensor(master, "master");
+  check_cuda_tensor(grad, "grad");
+  check_cuda_tensor(m, "m");
+  check_cuda_tensor(v, "v");
+  TDSV_CHECK(master.scalar_type() == at::kFloat, "adamw: fp32 master");
+  const int64_t n = master.numel();
+  TDSV_CHECK(grad.numel() == n && m.numel() == n && v.numel() == n, "adamw: size mismatch");
+  TDSV_CHECK(m.scalar_type() == v.scalar_type(), "adamw: moments share a dtype");
+  __nv_bfloat16* outp = nullptr;
+  if (out.has_value() && out->defined()) {
+    check_cuda_tensor(*out, "out");
+    TDSV_CHECK(out->scalar_type() == at::kBFloat16 && out->numel() == n, "adamw: bf16 out copy");
+    outp = reinterpret_cast<__nv_bfloat16*>(out->data_ptr());
+  }
+  const float* gsp = nullptr;
+  if (grad_scale_t.has_value() && grad_scale_t->defined()) gsp = grad_scale_t->data_ptr<float>();
+  if (n == 0) return;
+  const float bc1 = static_cast<float>(1.0 - std::pow(beta1, static_cast<double>(step)));
+  const float bc2s = static_cast<float>(std::sqrt(1.0 - std::pow(beta2, static_cast<double>(step))));
+  c10::cuda::CUDAGuard guard(master.device());
+  const int grid = grid_for(n);
+#define TDSV_ADAMW(GT, MT, gptr, mptr, vptr)                                                                   \
+  adamw_kernel<GT, MT><<<grid, 256, 0, stream()>>>(master.data_ptr<float>(), gptr, mptr, vptr, outp, n,       \
+                                                   static_cast<float>(lr), static_cast<float>(beta1),         \
+                                                   static_cast<float>(beta2), static_cast<float>(eps),        \
+                                                   static_cast<float>(weight_decay), bc1, bc2s,               \
+                                                   static_cast<float>(grad_scale), gsp)
+  const bool g32 = grad.scalar_type() == at::kFloat;
+  const bool m32 = m.scalar_type() == at::kFloat;
+  auto gbf = reinterpret_cast<const __nv_bfloat16*>(grad.data_ptr());
+  auto mbf = reinterpret_cast<__nv_bfloat16*>(m.data_ptr());
+  auto vbf = reinterpret_cast<__nv_bfloat16*>(v.data_ptr());
+  if (g32 && m32) TDSV_ADAMW(float, float, grad.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>());
+  else if (g32) TDSV_ADAMW(float, __nv_bfloat16, grad.data_ptr<float>(), mbf, vbf);
+  else if (m32) TDSV_ADAMW(__nv_bfloat16, float, gbf, m.data_ptr<float>(), v.data_ptr<float>());
+  else TDSV_ADAMW(__nv_bfloat16, __nv_bfloat16, gbf, mbf, vbf);
+#undef TDSV_ADAMW
+  TDSV_LAUNCH_CHECK();
+}
+
+void sgd_step(at::Tensor& param, const at::Tensor& grad, const c10::optional<at::Tensor>& out, double lr,
+              double grad_scale, const c10::optional<at::Tensor>& nonfinite) {
+  check_cuda_tensor(param, "param");
+  check_cuda_tensor(grad, "grad");
+  const int64_t n = param.numel();
+  TDSV_CHECK(grad.numel() == n, "sgd: size mismatch");
+  __nv_bfloat16* outp = nullptr;
+  if (out.has_value() && out->defined()) outp = reinterpret_cast<__nv_bfloat16*>(out->data_ptr());
+  int* flag = nullptr;
+  if (nonfinite.has_value() && nonfinite->defined()) flag = nonfinite->data_ptr<int>();
+  if (n == 0) return;
+  c10::cuda::CUDAGuard guard(param.device());
+  const int grid = grid_for(n);
+  const bool g32 = grad.scalar_type() == at::kFloat;
+  const bool p32 = param.scalar_type() == at::kFloat;
+  auto gbf = reinterpret_cast<const __nv_bfloat16*>(grad.data_ptr());
+  auto pbf = reinterpret_cast<__nv_bfloat16*>(param.data_ptr());
+  const float lrf = static_cast<float>(lr), gsf = static_cast<float>(grad_scale);
+  if (g32 && p32) sgd_kernel<float, float><<<grid, 256, 0, stream()>>>(param.data_ptr<float>(), grad.data_ptr<float>(), outp, n, lrf, gsf, flag);
+  else if (g32) sgd_kernel<float, __nv_bfloat16><<<grid, 256, 0, stream()>>>(pbf, grad.data_ptr<float>(), outp, n, lrf, gsf, flag);
+  else if (p32) sgd_kernel<__nv_bfloat16, float><<<grid, 256, 0, stream()>>>(param.data_ptr<float>(), gbf, outp, n, lrf, gsf, flag);
+  else sgd_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, 256, 0, stream()>>>(pbf, gbf, outp, n, lrf, gsf, flag);
+  TDSV_LAUNCH_CHECK();
+}
+
+at::Tensor column_sum(const at::Tensor& partial);
+
+// Sum of squares of a tensor as a 0-d fp32 device tensor (fixed-order reduction).
+at::Tensor grad_sq_norm(const at::Tensor& g) {
+  check_cuda_tensor(g, "g");
+  const int64_t n = g.numel();
+  const int grid = std::min(grid_for(n), 1024);
+  auto partial = at::empty({grid, 1}, g.options().dtype(at::kFloat));
+  c10::cuda::CUDAGuard guard(g.device());
+  if (g.scalar_type() == at::kFloat) {
+    sq_norm_kernel<float><<<grid, 256, 0, stream()>>>(g.data_ptr<float>(), partial.data_ptr<float>(), n);
+  } else {
+    TDSV_CHECK(g.scalar_type() == at::kBFloat16, "grad_sq_norm: fp32 or bf16");
+    sq_norm_kernel<__nv_bfloat16><<<grid, 256, 0, stream()>>>(reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()),
+                                                              partial.data_ptr<float>(), n);
+  }
+  TDSV_LAUNCH_CHECK();
+  return column_sum(partial).view({});
+}
+
+}  // namespace tdsv

@@ -1,0 +1,135 @@
+// SwiGLU activation for the expert MLPs, forward and backward.
+//
+// Qwen3 experts (dsv41_train/models/qwen/model.py:231-238): h = silu(gate) * up, with gate and up
+// the two halves of the gate_up projection ("split" layout, [R, 2I] = [gate | up]).
+// DSV4 experts (dsv41_train/models/dsv4/moe/kernels.py:15-27, 31-162): gate/up interleaved per
+// column ("interleaved" layout, [R, I, 2]); gate is clamped to <= limit, up to [-limit, limit],
+// SiLU(-inf) = 0, and the result is multiplied by the per-row route weight. The route-weight
+// gradient is a per-row dot product reduced in a fixed order (no atomics).
+#include "common.cuh"
+
+namespace tdsv {
+
+namespace {
+
+__device__ __forceinline__ void load_gu(const __nv_bfloat16* gu, int64_t row, int i, int inter, bool interleaved,
+                                        float& g, float& u) {
+  if (interleaved) {
+    const __nv_bfloat162 p = reinterpret_cast<const __nv_bfloat162*>(gu + row * 2 * inter)[i];
+    g = __low2float(p);
+    u = __high2float(p);
+  } else {
+    g = bf2f(gu[row * 2 * inter + i]);
+    u = bf2f(gu[row * 2 * inter + inter + i]);
+  }
+}
+
+__global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, const float* __restrict__ w,
+                                  __nv_bfloat16* __restrict__ out, int64_t rows, int inter, bool interleaved,
+                                  float limit) {
+  const int64_t row = blockIdx.x;
+  if (row >= rows) return;
+  const float ws = w != nullptr ? w[row] : 1.f;
+  for (int i = threadIdx.x; i < inter; i += blockDim.x) {
+    float g, u;
+    load_gu(gu, row, i, inter, interleaved, g, u);
+    if (limit > 0.f) {
+      g = fminf(g, limit);
+      u = fminf(fmaxf(u, -limit), limit);
+    }
+    const float s = (g == -INFINITY) ? 0.f : silu_f(g);
+    out[row * inter + i] = f2bf(s * u * ws);
+  }
+}
+
+__global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ gu,
+                                  const float* __restrict__ w, __nv_bfloat16* __restrict__ dgu,
+                                  float* __restrict__ dw, int64_t rows, int inter, bool interleaved, float limit) {
+  __shared__ float scratch[32];
+  const int64_t row = blockIdx.x;
+  if (row >= rows) return;
+  const float ws = w != nullptr ? w[row] : 1.f;
+  float dot = 0.f;
+  for (int i = threadIdx.x; i < inter; i += blockDim.x) {
+    float g0, u0;
+    load_gu(gu, row, i, inter, interleaved, g0, u0);
+    float g = g0, u = u0;
+    bool g_pass = true, u_pass = true;
+    if (limit > 0.f) {
+      g_pass = g0 <= limit;
+      u_pass = (u0 >= -limit) && (u0 <= limit);
+      g = fminf(g0, limit);
+      u = fminf(fmaxf(u0, -limit), limit);
+    }
+    const float d = bf2f(dout[row * inter + i]);
+    float s, ds;
+    if (g == -INFINITY) {
+      s = 0.f;
+      ds = 0.f;
+    } else {
+      const float sg = sigmoid_f(g);
+      s = g * sg;
+      ds = sg * (1.f + g * (1.f - sg));
+    }
+    dot += d * s * u;
+    const float dg = g_pass ? d * ws * u * ds : 0.f;
+    const float du = u_pass ? d * ws * s : 0.f;
+    if (interleaved) {
+      reinterpret_cast<__nv_bfloat162*>(dgu + row * 2 * inter)[i] = __floats2bfloat162_rn(dg, du);
+    } else {
+      dgu[row * 2 * inter + i] = f2bf(dg);
+      dgu[row * 2 * inter + inter + i] = f2bf(du);
+    }
+  }
+  if (dw != nullptr) {
+    dot = block_sum(dot, scratch);
+    if (threadIdx.x == 0) dw[row] = dot;
+  }
+}
+
+}  // namespace
+
+at::Tensor swiglu_fwd(const at::Tensor& gu, const c10::optional<at::Tensor>& w, bool interleaved, double limit) {
+  check_cuda_tensor(gu, "gate_up");
+  TDSV_CHECK(gu.scalar_type() == at::kBFloat16 && gu.dim() == 2 && gu.size(1) % 2 == 0, "swiglu: bf16 [R, 2I]");
+  const int64_t rows = gu.size(0);
+  const int inter = static_cast<int>(gu.size(1) / 2);
+  auto out = at::empty({rows, inter}, gu.options());
+  if (rows == 0) return out;
+  const float* wp = nullptr;
+  if (w.has_value() && w->defined()) {
+    check_cuda_tensor(*w, "w");
+    TDSV_CHECK(w->scalar_type() == at::kFloat && w->numel() == rows, "swiglu: fp32 weight per row");
+    wp = w->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard guard(gu.device());
+  const int threads = std::min(1024, std::max(32, ((inter + 31) / 32) * 32 / 2));
+  swiglu_fwd_kernel<<<rows, threads, 0, stream()>>>(reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), wp,
+                                                    reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, inter,
+                                                    interleaved, static_cast<float>(limit));
+  TDSV_LAUNCH_CHECK();
+  return out;
+}
+
+std::vector<at::Tensor> swiglu_bwd(const at::Tensor& dout, const at::Tensor& gu, const c10::optional<at::Tensor>& w,
+                                   bool interleaved, double limit, bool need_dw) {
+  check_cuda_tensor(dout, "dout");
+  check_cuda_tensor(gu, "gate_up");
+  const int64_t rows = gu.size(0);
+  const int inter = static_cast<int>(gu.size(1) / 2);
+  auto dgu = at::empty_like(gu);
+  auto dw = at::zeros({rows}, gu.options().dtype(at::kFloat));
+  if (rows == 0) return {dgu, dw};
+  const float* wp = nullptr;
+  if (w.has_value() && w->defined()) wp = w->data_ptr<float>();
+  c10::cuda::CUDAGuard guard(gu.device());
+  const int threads = std::min(1024, std::max(32, ((inter + 31) / 32) * 32 / 2));
+  swiglu_bwd_kernel<<<rows, threads, 0, stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), wp,
+      reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), need_dw ? dw.data_ptr<float>() : nullptr, rows, inter,
+      interleaved, static_cast<float>(limit));
+  TDSV_LAUNCH_CHECK();
+  return {dgu, dw};
+}
+
+}  // namespace tdsv

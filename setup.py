@@ -1,0 +1,47 @@
+"""Build the sm_100a CUDA extension in-tree: ``python setup.py build_ext --inplace``.
+
+The extension is compiled for Blackwell B200 only (``compute_100a`` / ``sm_100a``);
+there is no other architecture and no JIT fallback.
+"""
+
+import glob
+import os
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+SOURCES = sorted(glob.glob(os.path.join("csrc", "*.cu"))) + sorted(
+    glob.glob(os.path.join("csrc", "*.cpp"))
+)
+
+NVCC_FLAGS = [
+    "-O3",
+    "-lineinfo",
+    "-std=c++17",
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "--expt-relaxed-constexpr",
+    "-Xptxas", "-v" if os.environ.get("TDSV_PTXAS_VERBOSE") else "-O3",
+    "-DNDEBUG",
+    "-U__CUDA_NO_HALF_OPERATORS__",
+    "-U__CUDA_NO_HALF_CONVERSIONS__",
+    "-U__CUDA_NO_BFLOAT16_OPERATORS__",
+    "-U__CUDA_NO_BFLOAT16_CONVERSIONS__",
+]
+if os.environ.get("TDSV_BOUNDS_CHECK"):
+    NVCC_FLAGS.append("-DTDSV_BOUNDS_CHECK=1")
+
+setup(
+    name="tiny_dsv41_b200",
+    version="0.1.0",
+    packages=["tiny_dsv41_b200"],
+    ext_modules=[
+        CUDAExtension(
+            name="tiny_dsv41_b200._C",
+            sources=SOURCES,
+            include_dirs=[os.path.join(ROOT, "csrc")],
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+        )
+    ],
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

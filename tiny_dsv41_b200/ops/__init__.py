@@ -1,0 +1,17 @@
+"""Hot ops of the framework. CUDA tensors run the sm_100a kernels of ``tiny_dsv41_b200._C``;
+CPU tensors run the plain-PyTorch restatement used as the test oracle."""
+
+from ._ext import available, check_status, ext, on_gpu
+from .attention import causal_attention
+from .gemm import grouped_linear, linear, matmul_nt
+from .loss import linear_cross_entropy, token_log_probs
+from .moe import Routing, build_routing, combine, gather, swiglu
+from .norm import rms_norm
+from .rope import inv_freq, qk_norm_rope, rope_interleaved
+from .router import AuxGradient, route
+
+__all__ = [
+    "AuxGradient", "Routing", "available", "build_routing", "causal_attention", "check_status", "combine",
+    "ext", "gather", "grouped_linear", "inv_freq", "linear", "linear_cross_entropy", "matmul_nt", "on_gpu",
+    "qk_norm_rope", "rms_norm", "rope_interleaved", "route", "swiglu", "token_log_probs",
+]

@@ -1,0 +1,98 @@
+"""bf16 GEMMs on the persistent tcgen05 kernel (``csrc/gemm_tc.cu``).
+
+* :func:`linear` - ``y = x @ w.T`` with w in ``nn.Linear`` layout; backward uses the MN-major
+  operand forms (dx = dy @ w, dw = dy^T @ x) so no transposed copies are made.
+* :func:`grouped_linear` - expert-major grouped GEMM over 128-row aligned expert segments whose
+  offsets/sizes are device tensors (replaces ``torch._grouped_mm`` in
+  ``dsv41_train/models/dsv4/moe/module.py:78-99`` and the per-expert loop of
+  ``dsv41_train/models/qwen/model.py:231-238``).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ._ext import ext, on_gpu
+
+
+def _kernel_ok(*tensors: torch.Tensor) -> bool:
+    return all(t.dtype == torch.bfloat16 for t in tensors)
+
+
+def matmul_nt(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """a [M, K] @ b[N, K]^T on the tensor-core kernel."""
+    out = torch.empty(a.shape[0], b.shape[0], dtype=out_dtype, device=a.device)
+    ext().gemm(a.contiguous(), b.contiguous(), out, False, False, False)
+    return out
+
+
+class _Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight):
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).contiguous()
+        out = torch.empty(x2.shape[0], weight.shape[0], dtype=torch.bfloat16, device=x.device)
+        ext().gemm(x2, weight, out, False, False, False)
+        ctx.save_for_backward(x2, weight)
+        ctx.shape = shape
+        return out.view(*shape[:-1], weight.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):
+        x2, weight = ctx.saved_tensors
+        dy2 = dy.reshape(-1, weight.shape[0]).contiguous()
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty_like(x2)
+            ext().gemm(dy2, weight, dx, False, True, False)
+            dx = dx.view(ctx.shape)
+        if ctx.needs_input_grad[1]:
+            dw = torch.empty_like(weight)
+            ext().gemm(dy2, x2, dw, True, True, False)
+        return dx, dw
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+    if on_gpu(x) and _kernel_ok(x, weight) and weight.shape[0] % 8 == 0 and weight.shape[1] % 8 == 0:
+        return _Linear.apply(x, weight)
+    return torch.nn.functional.linear(x, weight.to(x.dtype))
+
+
+def grouped_linear_reference(x, weight, offsets, rows):
+    out = x.new_zeros(x.shape[0], weight.shape[1])
+    for g, (start, count) in enumerate(zip(offsets.tolist(), rows.tolist())):
+        if count:
+            out[start:start + count] = (x[start:start + count].float() @ weight[g].float().t()).to(x.dtype)
+    return out
+
+
+class _GroupedLinear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, weight, offsets, rows):
+        out = torch.empty(x.shape[0], weight.shape[1], dtype=torch.bfloat16, device=x.device)
+        ext().grouped_gemm_m(x, weight, offsets, rows, out, False, x.shape[0])
+        ctx.save_for_backward(x, weight, offsets, rows)
+        return out
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, weight, offsets, rows = ctx.saved_tensors
+        dy = dy.contiguous()
+        dx = dw = None
+        if ctx.needs_input_grad[0]:
+            dx = torch.empty_like(x)
+            ext().grouped_gemm_m(dy, weight, offsets, rows, dx, True, x.shape[0])
+        if ctx.needs_input_grad[1]:
+            dw = torch.empty_like(weight)
+            ext().grouped_gemm_k(dy, x, offsets, rows, dw, False)
+        return dx, dw, None, None
+
+
+def grouped_linear(x: torch.Tensor, weight: torch.Tensor, offsets: torch.Tensor, rows: torch.Tensor) -> torch.Tensor:
+    """Rows ``[offsets[g], offsets[g] + rows[g])`` of x times ``weight[g].T`` (weight [G, N, K]).
+
+    Row segments must be 128-aligned with zero padding rows (see ops.moe.build_routing).
+    """
+    if on_gpu(x) and _kernel_ok(x, weight):
+        return _GroupedLinear.apply(x.contiguous(), weight.contiguous(), offsets, rows)
+    return grouped_linear_reference(x, weight, offsets, rows)

@@ -1,0 +1,116 @@
+"""AdamW with fp32 master weights over bf16 compute parameters.
+
+Each parameter (or its local FSDP/DTensor shard) gets an fp32 master copy and two moments
+(fp32 by default, bf16 optionally). ``step()`` runs one fused kernel per tensor that applies
+decoupled weight decay, updates the moments with bias correction (``torch.optim.AdamW``
+semantics), writes the new master and the rounded bf16 parameter. With ``in_backward=True`` the
+update of a parameter runs from its post-accumulate-grad hook, so gradients never accumulate for
+the whole model (no global-norm clipping in that mode).
+
+On CPU the same math runs in plain PyTorch.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ..ops import ext
+from ..runtime import local_tensor
+
+
+class FusedAdamW:
+    def __init__(self, params, lr: float = 1e-4, betas=(0.9, 0.999), eps: float = 1e-8,
+                 weight_decay: float = 0.01, *, moment_dtype: torch.dtype = torch.float32,
+                 in_backward: bool = False, grad_scale: float = 1.0) -> None:
+        self.params = [p for p in params if p.requires_grad]
+        self.lr, self.betas, self.eps, self.weight_decay = lr, betas, eps, weight_decay
+        self.moment_dtype = moment_dtype
+        self.grad_scale = grad_scale
+        self.step_count = 0
+        self.state: dict[int, dict[str, torch.Tensor]] = {}
+        for p in self.params:
+            local = local_tensor(p.data)
+            self.state[id(p)] = {
+                "master": local.detach().float().clone(),
+                "m": torch.zeros(local.shape, dtype=moment_dtype, device=local.device),
+                "v": torch.zeros(local.shape, dtype=moment_dtype, device=local.device),
+            }
+        self.in_backward = in_backward
+        self._hooks = []
+        self._pending_step = False
+        if in_backward:
+            for p in self.params:
+                self._hooks.append(p.register_post_accumulate_grad_hook(self._hook))
+
+    # -- public API ----------------------------------------------------------------------------
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        for p in self.params:
+            p.grad = None
+
+    def begin_step(self) -> None:
+        """In-backward mode: advance the step counter before the backward that applies it."""
+        self.step_count += 1
+
+    def step(self, clip_coefficient: torch.Tensor | None = None) -> None:
+        if self.in_backward:
+            return
+        self.step_count += 1
+        for p in self.params:
+            if p.grad is not None:
+                self._update(p, clip_coefficient)
+
+    def state_dict(self) -> dict:
+        return {"step": self.step_count, "lr": self.lr, "betas": self.betas, "eps": self.eps,
+                "weight_decay": self.weight_decay,
+                "state": [{k: v for k, v in self.state[id(p)].items()} for p in self.params]}
+
+    def load_state_dict(self, state: dict) -> None:
+        self.step_count = int(state["step"])
+        for p, saved in zip(self.params, state["state"]):
+            for key in ("master", "m", "v"):
+                self.state[id(p)][key].copy_(saved[key])
+
+    def remove_hooks(self) -> None:
+        for hook in self._hooks:
+            hook.remove()
+        self._hooks = []
+
+    # -- internals -----------------------------------------------------------------------------
+    def _hook(self, p: torch.Tensor) -> None:
+        if self.step_count == 0:
+            self.step_count = 1
+        self._update(p, None)
+        p.grad = None
+
+    @torch.no_grad()
+    def _update(self, p: torch.Tensor, clip_coefficient: torch.Tensor | None) -> None:
+        st = self.state[id(p)]
+        grad = local_tensor(p.grad)
+        data = local_tensor(p.data)
+        beta1, beta2 = self.betas
+        if data.is_cuda:
+            out = data if data.dtype == torch.bfloat16 else None
+            ext().adamw_step(st["master"], grad.contiguous(), st["m"], st["v"], out, self.lr, beta1, beta2,
+                             self.eps, self.weight_decay, self.step_count, self.grad_scale, clip_coefficient)
+            if out is None:
+                data.copy_(st["master"])
+            return
+        g = grad.float() * self.grad_scale
+        if clip_coefficient is not None:
+            g = g * clip_coefficient
+        master = st["master"]
+        master.mul_(1 - self.lr * self.weight_decay)
+        m = st["m"].float().mul_(beta1).add_(g, alpha=1 - beta1)
+        v = st["v"].float().mul_(beta2).addcmul_(g, g, value=1 - beta2)
+        bc1 = 1 - beta1 ** self.step_count
+        bc2 = 1 - beta2 ** self.step_count
+        denom = (v.sqrt() / math.sqrt(bc2)).add_(self.eps)
+        master.addcdiv_(m, denom, value=-self.lr / bc1)
+        st["m"].copy_(m)
+        st["v"].copy_(v)
+        data.copy_(master)
+
+
+__all__ = ["FusedAdamW"]

@@ -1,0 +1,236 @@
+"""Qwen3-MoE full-parameter trainer (the public training API) and its benchmark harness.
+
+:class:`QwenTrainer` builds the model directly on the GPU (meta-device construction, then
+random init on the device), shards dense weights with FSDP2 over the world and places experts
+with EP, and runs AdamW with fp32 master weights applied inside the backward pass.
+``train_step(input_ids, labels)`` is one optimizer step; inputs may live on the host (pinned) or
+the device.
+
+:class:`QwenSFTBench` times it the way ``bench.py`` reports: device time of exactly K steps
+(CUDA events, barrier + synchronize on both sides, max over ranks) and an end-to-end wall time
+through ``train_step`` including the per-step host-to-device input copy and loss read-back.
+"""
+
+from __future__ import annotations
+
+import os
+import time
+
+import torch
+import torch.distributed as dist
+
+from ..models.qwen import Qwen3MoeConfig, Qwen3MoeForCausalLM
+from ..models.qwen.model import Qwen3MoeExperts
+from ..optim import FusedAdamW
+from ..parallel.cp import ContextParallel
+from ..parallel.dispatch import AllToAllTokenDispatcher, TokenDispatcher
+from ..runtime import initialize_runtime
+
+
+def _init_on_device(model: Qwen3MoeForCausalLM, seed: int, rank: int) -> None:
+    gen = torch.Generator(device="cuda")
+    std = model.config.initializer_range
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if name.endswith("norm.weight") or "layernorm" in name:
+                p.fill_(1.0)
+            elif name.endswith("bias"):
+                p.zero_()
+            else:
+                is_expert = ".experts." in name
+                gen.manual_seed(seed + (1000003 * (rank + 1) if is_expert else 0) + hash(name) % 100003)
+                p.normal_(0.0, std, generator=gen)
+
+
+class QwenTrainer:
+    def __init__(self, config: Qwen3MoeConfig, *, lr: float = 1e-5, moment_dtype=torch.float32,
+                 dispatcher: str = "auto", gradient_checkpointing: bool = True, seed: int = 0) -> None:
+        self.runtime = initialize_runtime(require_distributed=int(os.environ.get("WORLD_SIZE", "1")) > 1,
+                                          timeout_seconds=900)
+        rt = self.runtime
+        torch.manual_seed(seed)
+        self.world = rt.world_size
+        self.meshes = None
+        cp = ContextParallel()
+        if self.world > 1:
+            from ..parallel.meshes import ParallelMeshes
+
+            self.meshes = ParallelMeshes.build(cp=1, ep=self.world)
+            token_dispatcher = self._make_dispatcher(dispatcher)
+        else:
+            token_dispatcher = TokenDispatcher()
+        with torch.device("meta"):
+            model = Qwen3MoeForCausalLM(config, cp, token_dispatcher)
+        model = model.to_empty(device=rt.device).to(torch.bfloat16)
+        model.model.rope_inv_freq = model.model.rope_inv_freq.float()
+        from ..ops.rope import inv_freq
+
+        model.model.rope_inv_freq = inv_freq(config.head_dim, config.rope_theta, rt.device)
+        _init_on_device(model, seed, rt.rank)
+        if gradient_checkpointing:
+            model.gradient_checkpointing_enable()
+        model.train()
+        self.expert_params = [p for m in model.modules() if isinstance(m, Qwen3MoeExperts) for p in m.parameters()]
+        expert_ids = {id(p) for p in self.expert_params}
+        if self.world > 1:
+            self._apply_fsdp(model)
+        self.model = model
+        dense = [p for p in model.parameters() if id(p) not in expert_ids]
+        self.optimizers = [
+            FusedAdamW(dense, lr=lr, betas=(0.9, 0.95), weight_decay=0.1, moment_dtype=moment_dtype, in_backward=True),
+            FusedAdamW(self.expert_params, lr=lr, betas=(0.9, 0.95), weight_decay=0.1, moment_dtype=moment_dtype,
+                       in_backward=True, grad_scale=1.0 / self.world),
+        ]
+
+    def _make_dispatcher(self, kind: str):
+        if kind in ("auto", "nvlink"):
+            try:
+                from ..parallel.nvlink_ep import NVLinkTokenDispatcher
+
+                return NVLinkTokenDispatcher(self.meshes.ep)
+            except ImportError:
+                if kind == "nvlink":
+                    raise
+        return AllToAllTokenDispatcher(self.meshes.ep)
+
+    def _apply_fsdp(self, model) -> None:
+        from torch.distributed.fsdp import MixedPrecisionPolicy, fully_shard
+
+        policy = MixedPrecisionPolicy(param_dtype=torch.bfloat16, reduce_dtype=torch.float32)
+        mesh = self.meshes.fsdp
+        ignored = set(self.expert_params)
+        opts = {"mesh": mesh, "mp_policy": policy, "reshard_after_forward": True}
+        fully_shard(model.model.embed_tokens, **opts)
+        for layer in model.model.layers:
+            fully_shard(layer, ignored_params=ignored, **opts)
+        fully_shard(model.lm_head, **opts)
+        fully_shard(model, ignored_params=ignored, **opts)
+
+    def train_step(self, input_ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        device = self.runtime.device
+        input_ids = input_ids.to(device, non_blocking=True)
+        labels = labels.to(device, non_blocking=True)
+        for opt in self.optimizers:
+            opt.begin_step()
+        out = self.model(input_ids, labels=labels, output_router_logits=True)
+        out.loss.backward()
+        return out.loss.detach()
+
+    def close(self) -> None:
+        for opt in self.optimizers:
+            opt.remove_hooks()
+        if dist.is_initialized():
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+class QwenSFTBench:
+    def __init__(self, args) -> None:
+        self.args = args
+        config = Qwen3MoeConfig(num_hidden_layers=args.layers)
+        moment = torch.float32 if args.moment_dtype == "fp32" else torch.bfloat16
+        self.trainer = QwenTrainer(config, lr=args.lr, moment_dtype=moment, dispatcher=args.dispatcher)
+        self.config = config
+
+    def _batch(self, gen: torch.Generator):
+        a = self.args
+        ids = torch.randint(0, self.config.vocab_size, (a.batch_size, a.seq_len), generator=gen)
+        ids[:, 0] = self.config.bos_token_id
+        labels = ids.clone()
+        labels[:, : a.seq_len // 2] = -100  # loss on the last 50% of tokens
+        return ids.pin_memory(), labels.pin_memory()
+
+    def _count_launches(self, batches) -> dict:
+        """Kernels launched in one (extra, untimed) step, split into this repo's and others."""
+        from torch.profiler import ProfilerActivity, profile
+
+        ids, labels = batches[0]
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            self.trainer.train_step(ids, labels)
+            torch.cuda.synchronize()
+        own = other = 0
+        for evt in prof.events():
+            if evt.device_type == torch.autograd.DeviceType.CUDA:
+                if "tdsv" in evt.name:
+                    own += 1
+                else:
+                    other += 1
+        return {"own": own, "other": other}
+
+    def run(self) -> dict:
+        import sys
+
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+        from bench import ClockSampler
+
+        a = self.args
+        t = self.trainer
+        rt = t.runtime
+        gen = torch.Generator().manual_seed(1234 + rt.rank)
+        batches = [self._batch(gen) for _ in range(4)]
+        # L2 flush buffer (larger than the 126 MB L2) written between timed steps
+        flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=rt.device)
+        for i in range(a.warmup):
+            t.train_step(*batches[i % len(batches)])
+        torch.cuda.synchronize()
+        launches = self._count_launches(batches)
+
+        def barrier():
+            if dist.is_initialized():
+                dist.barrier()
+            torch.cuda.synchronize()
+
+        # device-timed region: exactly K steps
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        losses = []
+        with ClockSampler(rt.local_rank) as clocks:
+            barrier()
+            start.record()
+            for i in range(a.steps):
+                flush.zero_()
+                losses.append(t.train_step(*batches[i % len(batches)]))
+            end.record()
+            barrier()
+        device_ms = start.elapsed_time(end)
+        # end-to-end through the public API: H2D of inputs, D2H of the loss every step
+        barrier()
+        wall0 = time.perf_counter()
+        e2e_losses = []
+        for i in range(a.steps):
+            loss = t.train_step(*batches[i % len(batches)])
+            e2e_losses.append(loss.item())
+        torch.cuda.synchronize()
+        wall_s = time.perf_counter() - wall0
+        times = torch.tensor([device_ms, wall_s * 1000.0], device=rt.device)
+        if dist.is_initialized():
+            dist.all_reduce(times, op=dist.ReduceOp.MAX)
+        device_ms, wall_ms = times.tolist()
+        tokens = a.batch_size * a.seq_len * rt.world_size * a.steps
+        value = tokens / (device_ms / 1000.0)
+        e2e = tokens / (wall_ms / 1000.0)
+        final_loss = float(losses[-1].item())
+        return {
+            "value": value,
+            "ms_per_step": device_ms / a.steps,
+            "e2e": {"value": e2e, "unit": "tokens/s", "ms_per_step": wall_ms / a.steps,
+                    "h2d_bytes_per_step": 2 * a.batch_size * a.seq_len * 8, "d2h_bytes_per_step": 4},
+            "gpu_launches": launches["own"] * a.steps,
+            "other_launches_per_step": launches["other"],
+            "loss": final_loss,
+            "e2e_last_loss": e2e_losses[-1],
+            "clocks": clocks.summary(),
+            "config": {
+                "model": MODEL_NAME if self.config.num_hidden_layers == 48 else f"REDUCED {self.config.num_hidden_layers}L (not the benchmark)",
+                "global_batch": a.batch_size * rt.world_size, "seq_len": a.seq_len,
+                "parallelism": f"ep{rt.world_size}+fsdp{rt.world_size}" if rt.world_size > 1 else "single-gpu",
+                "optimizer": f"AdamW in-backward, fp32 master, {a.moment_dtype} moments",
+                "grad_ckpt": True, "l2": "256 MB buffer written between timed steps",
+                "loss_tokens": "last 50%",
+            },
+        }
+
+    def close(self) -> None:
+        self.trainer.close()
+
+
+MODEL_NAME = "Qwen3-30B-A3B-shaped (48L, H2048, 32q/4kv x128, 128 experts top-8, I768, V151936)"
