@@ -99,7 +99,7 @@ def memory_plan(args, world: int) -> tuple[bool, str]:
     """Whether the full optimizer state fits in HBM at this N (fp32 master + moments per rank)."""
     from tiny_dsv41_b200.models.qwen import Qwen3MoeConfig
 
-    cfg = Qwen3MoeConfig(num_hidden_layers=args.layers)
+    cfg = Qwen3MoeConfig(num_hidden_layers=args.layers, max_window_layers=args.layers)
     experts = cfg.num_hidden_layers * cfg.num_experts * 3 * cfg.hidden_size * cfg.moe_intermediate_size
     dense = (cfg.num_hidden_layers * (cfg.hidden_size * (cfg.num_attention_heads + 2 * cfg.num_key_value_heads)
                                       * cfg.head_dim * 2 + cfg.hidden_size * cfg.num_experts)

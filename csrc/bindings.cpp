@@ -1,7 +1,34 @@
 // Python bindings of the sm_100a kernels (module tiny_dsv41_b200._C).
+#include <execinfo.h>
+#include <signal.h>
 #include <torch/extension.h>
+#include <unistd.h>
 
+#include <cstdlib>
 #include <vector>
+
+namespace {
+// Debug aid (TDSV_SEGV_BACKTRACE=1): print the native stack of a crashing thread to stderr.
+void segv_handler(int sig) {
+  void* frames[64];
+  const int n = backtrace(frames, 64);
+  const char msg[] = "tiny_dsv41_b200: native backtrace of the faulting thread:\n";
+  ssize_t ignored = write(STDERR_FILENO, msg, sizeof(msg) - 1);
+  (void)ignored;
+  backtrace_symbols_fd(frames, n, STDERR_FILENO);
+  signal(sig, SIG_DFL);
+  raise(sig);
+}
+void maybe_install_segv_handler() {
+  const char* flag = std::getenv("TDSV_SEGV_BACKTRACE");
+  if (flag != nullptr && flag[0] == '1') {
+    struct sigaction sa {};
+    sa.sa_handler = segv_handler;
+    sigemptyset(&sa.sa_mask);
+    sigaction(SIGSEGV, &sa, nullptr);
+  }
+}
+}  // namespace
 
 namespace tdsv {
 // status
@@ -56,10 +83,19 @@ void grouped_gemm_m(const at::Tensor& a, const at::Tensor& b, const at::Tensor& 
                     const at::Tensor& group_rows, at::Tensor& out, bool b_mn, int64_t max_rows);
 void grouped_gemm_k(const at::Tensor& a, const at::Tensor& b, const at::Tensor& group_off,
                     const at::Tensor& group_rows, at::Tensor& out, bool accumulate);
+// mhc.cu
+at::Tensor mhc_sinkhorn_fwd(const at::Tensor& comb, int64_t iters, double eps);
+at::Tensor mhc_sinkhorn_bwd(const at::Tensor& comb, const at::Tensor& grad, int64_t iters, double eps);
+at::Tensor mhc_collapse_fwd(const at::Tensor& s, const at::Tensor& w);
+std::vector<at::Tensor> mhc_collapse_bwd(const at::Tensor& g, const at::Tensor& s, const at::Tensor& w);
+at::Tensor mhc_expand_fwd(const at::Tensor& v, const at::Tensor& r, const at::Tensor& post, const at::Tensor& comb);
+std::vector<at::Tensor> mhc_expand_bwd(const at::Tensor& g, const at::Tensor& v, const at::Tensor& r,
+                                       const at::Tensor& post, const at::Tensor& comb);
 }  // namespace tdsv
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "tiny_dsv41_b200 sm_100a kernels";
+  maybe_install_segv_handler();
   m.def("read_status", &tdsv::read_status, "read and clear the device pipeline status word");
   m.def("rmsnorm_fwd", &tdsv::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &tdsv::rmsnorm_bwd);
@@ -84,4 +120,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &tdsv::gemm);
   m.def("grouped_gemm_m", &tdsv::grouped_gemm_m);
   m.def("grouped_gemm_k", &tdsv::grouped_gemm_k);
+  m.def("mhc_sinkhorn_fwd", &tdsv::mhc_sinkhorn_fwd);
+  m.def("mhc_sinkhorn_bwd", &tdsv::mhc_sinkhorn_bwd);
+  m.def("mhc_collapse_fwd", &tdsv::mhc_collapse_fwd);
+  m.def("mhc_collapse_bwd", &tdsv::mhc_collapse_bwd);
+  m.def("mhc_expand_fwd", &tdsv::mhc_expand_fwd);
+  m.def("mhc_expand_bwd", &tdsv::mhc_expand_bwd);
 }

@@ -358,8 +358,22 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// The driver API needs a current context; a fresh host thread (the autograd engine's worker,
+// a Python thread) has none until a runtime call binds the primary context of its device.
+void bind_primary_context() {
+  static thread_local int bound_device = -1;
+  int dev = 0;
+  TDSV_CUDA_CHECK(cudaGetDevice(&dev));
+  if (bound_device != dev) {
+    TDSV_CUDA_CHECK(cudaSetDevice(dev));
+    TDSV_CUDA_CHECK(cudaFree(nullptr));
+    bound_device = dev;
+  }
+}
+
 // Row-major bf16 tensor [outer..., rows, inner] with a box of {64 inner, box_rows rows, 1...}.
 CUtensorMap make_map(const at::Tensor& t, int box_rows) {
+  bind_primary_context();
   TDSV_CHECK(t.scalar_type() == at::kBFloat16, "gemm operands must be bf16");
   TDSV_CHECK(t.is_contiguous(), "gemm operands must be contiguous");
   TDSV_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, "gemm operand base must be 16-byte aligned");

@@ -28,6 +28,15 @@ NVCC_FLAGS = [
     "-U__CUDA_NO_BFLOAT16_OPERATORS__",
     "-U__CUDA_NO_BFLOAT16_CONVERSIONS__",
 ]
+# Link the shared libstdc++ (the one torch uses): the toolchain wrapper's own search path only
+# offers a dangling libstdc++.so symlink and would otherwise fall back to the static archive,
+# giving the extension a private iostream/locale copy.
+LINK_ARGS = []
+for candidate in ("/usr/lib/gcc/x86_64-linux-gnu/13", "/usr/lib/gcc/x86_64-linux-gnu/12"):
+    if os.path.exists(os.path.join(candidate, "libstdc++.so")):
+        LINK_ARGS.append("-L" + candidate)
+        break
+
 if os.environ.get("TDSV_BOUNDS_CHECK"):
     NVCC_FLAGS.append("-DTDSV_BOUNDS_CHECK=1")
 
@@ -41,6 +50,7 @@ setup(
             sources=SOURCES,
             include_dirs=[os.path.join(ROOT, "csrc")],
             extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
+            extra_link_args=LINK_ARGS,
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},

@@ -26,9 +26,20 @@ class AuxGradient:
 
     def __init__(self) -> None:
         self.vector: torch.Tensor | None = None
+        self.token_scale: torch.Tensor | None = None
 
-    def set(self, vector: torch.Tensor | None) -> None:
+    def set(self, vector: torch.Tensor | None, token_scale: torch.Tensor | None = None) -> None:
+        """``vector`` [E]; optional ``token_scale`` [T] (0 for masked tokens)."""
         self.vector = None if vector is None else vector.float().contiguous()
+        self.token_scale = None if token_scale is None else token_scale.float().reshape(-1, 1)
+
+    def softmax_gradient(self, logits: torch.Tensor) -> torch.Tensor:
+        """d aux / d logits through softmax(logits), in fp32."""
+        p = torch.softmax(logits.float(), dim=-1)
+        extra = p * (self.vector - (p * self.vector).sum(-1, keepdim=True))
+        if self.token_scale is not None:
+            extra = extra * self.token_scale
+        return extra
 
 
 def _scores_reference(logits: torch.Tensor, func: str) -> torch.Tensor:
@@ -65,9 +76,12 @@ class _Route(torch.autograd.Function):
         func, normalize, norm_eps, scale, aux = ctx.meta
         if dweights is None:
             dweights = torch.zeros(ids.shape, dtype=torch.float32, device=ids.device)
-        vector = aux.vector if aux is not None else None
+        fused = aux is not None and aux.vector is not None and aux.token_scale is None
+        vector = aux.vector if fused else None
         dlogits = ext().router_bwd(dweights.float().contiguous(), ids, scores, logits.contiguous(), vector,
                                    SCORE_FUNCS[func], normalize, float(norm_eps), float(scale))
+        if aux is not None and aux.vector is not None and not fused:
+            dlogits = (dlogits.float() + aux.softmax_gradient(logits)).to(dlogits.dtype)
         return dlogits, None, None, None, None, None, None, None
 
 
@@ -83,12 +97,9 @@ class _AuxHook(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad):
         (logits,) = ctx.saved_tensors
-        vector = ctx.aux.vector
-        if vector is None:
+        if ctx.aux.vector is None:
             return grad, None
-        p = torch.softmax(logits.float(), dim=-1)
-        extra = p * (vector - (p * vector).sum(-1, keepdim=True))
-        return grad + extra.to(grad.dtype), None
+        return grad + ctx.aux.softmax_gradient(logits).to(grad.dtype), None
 
 
 def route(

@@ -1,0 +1,65 @@
+"""DSV4 sparse attention (sliding window + selected compressed KV + per-head sink logit) and the
+sparse-indexer scores.
+
+``sparse_attention(q [B,H,L,D], kv [B,S,D], window_idx [B,L,W], window_mask [B,L,W],
+compressed [B,C,D] | None, compressed_idx [B,L,K] | None, sinks [H])`` returns [B,L,H,D]; the
+softmax runs over window logits, selected compressed logits and the sink logit together, and the
+sink contributes no value (``dsv41_train/models/dsv4/attention/module.py:473-534`` and the Triton
+K1/K2 kernels of ``sparse_attention.py``).
+
+``index_scores`` = sum_h w[q,h] * relu(q_h . k) * d^-1/2 over each query's visible compressed
+keys (``sparse_indexer.py:156-172``), -inf outside [start, end) or outside the candidate mask.
+
+Both are written as gathered batched matmuls (cuBLAS through PyTorch) in this module; the
+tcgen05 kernels for the 64-head x 512-dim MQA tile are a planned replacement behind the same
+signatures.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+
+def sparse_attention(query, kv, window_indices, window_mask, compressed_kv, compressed_indices, sinks, *,
+                     dropout: float = 0.0, deterministic: bool = False):
+    batch, heads, length, dim = query.shape
+    rows = torch.arange(batch, device=query.device).view(-1, 1, 1)
+    window_kv = kv[rows, window_indices.long()]  # [B, L, W, D]
+    scale = dim ** -0.5
+    logits = torch.einsum("bhld,blwd->bhlw", query, window_kv.to(query.dtype)) * scale
+    logits = logits.masked_fill(~window_mask.unsqueeze(1), torch.finfo(logits.dtype).min)
+    window = logits.shape[-1]
+    selected = None
+    if compressed_kv is not None and compressed_indices is not None:
+        valid = compressed_indices >= 0
+        selected = compressed_kv[rows, compressed_indices.clamp_min(0).long()]
+        picked = torch.einsum("bhsd,bskd->bhsk", query, selected.to(query.dtype)) * scale
+        picked = picked.masked_fill(~valid.unsqueeze(1), float("-inf"))
+        logits = torch.cat((logits, picked), dim=-1)
+    sink = sinks.float().view(1, -1, 1, 1).expand(batch, -1, length, -1)
+    combined = torch.cat((logits.float(), sink), dim=-1)
+    combined = combined - combined.max(dim=-1, keepdim=True).values
+    probs = torch.softmax(combined, dim=-1)[..., :-1]
+    probs = F.dropout(probs, dropout, dropout > 0).to(kv.dtype)
+    out = torch.einsum("bhlw,blwd->bhld", probs[..., :window], window_kv)
+    if selected is not None:
+        out = out + torch.einsum("bhsk,bskd->bhsd", probs[..., window:], selected.to(probs.dtype))
+    return out.transpose(1, 2).contiguous()
+
+
+def index_scores(query, keys, weights, starts, ends, width, candidates=None):
+    if width == 0:
+        return query.new_empty((*query.shape[:2], 0), dtype=torch.float32)
+    idx = starts.unsqueeze(-1) + torch.arange(width, device=query.device)
+    valid = idx < ends.unsqueeze(-1)
+    if candidates is not None:
+        valid = valid & candidates
+    rows = torch.arange(query.shape[0], device=query.device)[:, None, None]
+    gathered = keys[rows, idx.clamp_max(keys.shape[1] - 1)]
+    dots = torch.einsum("blhd,blkd->blkh", query.float(), gathered.float())
+    scores = (dots.relu() * query.shape[-1] ** -0.5 * weights.float().unsqueeze(2)).sum(-1)
+    return scores.masked_fill(~valid, float("-inf"))
+
+
+__all__ = ["index_scores", "sparse_attention"]

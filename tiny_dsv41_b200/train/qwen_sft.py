@@ -127,7 +127,7 @@ class QwenTrainer:
 class QwenSFTBench:
     def __init__(self, args) -> None:
         self.args = args
-        config = Qwen3MoeConfig(num_hidden_layers=args.layers)
+        config = Qwen3MoeConfig(num_hidden_layers=args.layers, max_window_layers=args.layers)
         moment = torch.float32 if args.moment_dtype == "fp32" else torch.bfloat16
         self.trainer = QwenTrainer(config, lr=args.lr, moment_dtype=moment, dispatcher=args.dispatcher)
         self.config = config
