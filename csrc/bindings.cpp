@@ -55,15 +55,17 @@ at::Tensor router_bwd(const at::Tensor& dweights, const at::Tensor& ids, const a
                       const at::Tensor& logits, const c10::optional<at::Tensor>& aux_coef, int64_t func,
                       bool normalize, double norm_eps, double scale);
 // moe_permute.cu
-at::Tensor moe_gather(const at::Tensor& x, const at::Tensor& src);
+at::Tensor moe_gather(const at::Tensor& x, const at::Tensor& src, const c10::optional<at::Tensor>& row_limit);
 at::Tensor moe_combine(const at::Tensor& rows, const at::Tensor& idx, const c10::optional<at::Tensor>& w);
 std::vector<at::Tensor> moe_combine_bwd(const at::Tensor& dout, const at::Tensor& rows, const at::Tensor& idx,
                                         const c10::optional<at::Tensor>& w, bool need_dw);
-void moe_zero_padding(at::Tensor& buf, const at::Tensor& src);
+void moe_zero_padding(at::Tensor& buf, const at::Tensor& src, const c10::optional<at::Tensor>& row_limit);
 // swiglu.cu
-at::Tensor swiglu_fwd(const at::Tensor& gu, const c10::optional<at::Tensor>& w, bool interleaved, double limit);
+at::Tensor swiglu_fwd(const at::Tensor& gu, const c10::optional<at::Tensor>& w, bool interleaved, double limit,
+                      const c10::optional<at::Tensor>& row_limit);
 std::vector<at::Tensor> swiglu_bwd(const at::Tensor& dout, const at::Tensor& gu, const c10::optional<at::Tensor>& w,
-                                   bool interleaved, double limit, bool need_dw);
+                                   bool interleaved, double limit, bool need_dw,
+                                   const c10::optional<at::Tensor>& row_limit);
 // loss.cu
 std::vector<at::Tensor> cross_entropy_fused(at::Tensor& logits, const at::Tensor& targets, double scale,
                                             int64_t ignore_index, bool write_grad);
@@ -91,6 +93,22 @@ std::vector<at::Tensor> mhc_collapse_bwd(const at::Tensor& g, const at::Tensor& 
 at::Tensor mhc_expand_fwd(const at::Tensor& v, const at::Tensor& r, const at::Tensor& post, const at::Tensor& comb);
 std::vector<at::Tensor> mhc_expand_bwd(const at::Tensor& g, const at::Tensor& v, const at::Tensor& r,
                                        const at::Tensor& post, const at::Tensor& comb);
+// ep_nvlink.cu
+void ep_wait(const at::Tensor& flags, int64_t epoch);
+void ep_signal(const at::Tensor& peer_flags, const c10::optional<at::Tensor>& peer_counts,
+               const c10::optional<at::Tensor>& counts, int64_t my_rank, int64_t epoch);
+void ep_push_rows(const at::Tensor& x, const at::Tensor& dest_mask, const at::Tensor& slot,
+                  const at::Tensor& peer_recv, const c10::optional<at::Tensor>& peer_meta,
+                  const c10::optional<at::Tensor>& ids, const c10::optional<at::Tensor>& weights, int64_t t_cap,
+                  int64_t e_local, at::Tensor& done_counter, const at::Tensor& peer_flags,
+                  const c10::optional<at::Tensor>& peer_counts, const c10::optional<at::Tensor>& counts,
+                  int64_t my_rank, int64_t epoch);
+void ep_combine_push(const at::Tensor& y, const at::Tensor& route, const c10::optional<at::Tensor>& weights,
+                     const at::Tensor& counts, const at::Tensor& peer_ret, const c10::optional<at::Tensor>& row_extra,
+                     const c10::optional<at::Tensor>& peer_retw, int64_t t_cap, at::Tensor& done_counter,
+                     const at::Tensor& peer_flags, int64_t my_rank, int64_t epoch);
+at::Tensor ep_reduce_returned(const at::Tensor& ret, const at::Tensor& dest_mask, const at::Tensor& slot,
+                              int64_t tokens);
 }  // namespace tdsv
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -126,4 +144,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mhc_collapse_bwd", &tdsv::mhc_collapse_bwd);
   m.def("mhc_expand_fwd", &tdsv::mhc_expand_fwd);
   m.def("mhc_expand_bwd", &tdsv::mhc_expand_bwd);
+  m.def("ep_wait", &tdsv::ep_wait);
+  m.def("ep_signal", &tdsv::ep_signal);
+  m.def("ep_push_rows", &tdsv::ep_push_rows);
+  m.def("ep_combine_push", &tdsv::ep_combine_push);
+  m.def("ep_reduce_returned", &tdsv::ep_reduce_returned);
 }

@@ -17,11 +17,12 @@ namespace tdsv {
 namespace {
 
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, const int32_t* __restrict__ src,
-                                   __nv_bfloat16* __restrict__ out, int64_t rows, int h) {
+                                   __nv_bfloat16* __restrict__ out, int64_t rows, int h,
+                                   const int32_t* __restrict__ row_limit) {
   // one warp per row, 16B vectors
   const int lane = threadIdx.x & 31;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (r >= rows) return;
+  if (r >= rows || (row_limit != nullptr && r >= *row_limit)) return;
   const int s = src[r];
   const int vecs = h / 8;
   bf16x8* dst = reinterpret_cast<bf16x8*>(out + r * h);
@@ -92,10 +93,10 @@ __global__ void combine_rows_bwd_kernel(const __nv_bfloat16* __restrict__ dout, 
 
 // Zero the padding rows of the expert-major buffer (rows whose source index is negative).
 __global__ void zero_rows_kernel(__nv_bfloat16* __restrict__ buf, const int32_t* __restrict__ src, int64_t rows,
-                                 int h) {
+                                 int h, const int32_t* __restrict__ row_limit) {
   const int lane = threadIdx.x & 31;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (r >= rows || src[r] >= 0) return;
+  if (r >= rows || (row_limit != nullptr && r >= *row_limit) || src[r] >= 0) return;
   bf16x8 z;
 #pragma unroll
   for (int i = 0; i < 4; ++i) z.v[i] = __floats2bfloat162_rn(0.f, 0.f);
@@ -105,7 +106,11 @@ __global__ void zero_rows_kernel(__nv_bfloat16* __restrict__ buf, const int32_t*
 
 }  // namespace
 
-at::Tensor moe_gather(const at::Tensor& x, const at::Tensor& src) {
+static const int32_t* limit_ptr(const c10::optional<at::Tensor>& t) {
+  return (t.has_value() && t->defined()) ? t->data_ptr<int32_t>() : nullptr;
+}
+
+at::Tensor moe_gather(const at::Tensor& x, const at::Tensor& src, const c10::optional<at::Tensor>& row_limit) {
   check_cuda_tensor(x, "x");
   check_cuda_tensor(src, "src");
   TDSV_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 2, "moe_gather: x must be bf16 [T, H]");
@@ -118,7 +123,7 @@ at::Tensor moe_gather(const at::Tensor& x, const at::Tensor& src) {
   c10::cuda::CUDAGuard guard(x.device());
   gather_rows_kernel<<<(rows + 7) / 8, 256, 0, stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), src.data_ptr<int32_t>(),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, h);
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, h, limit_ptr(row_limit));
   TDSV_LAUNCH_CHECK();
   return out;
 }
@@ -173,7 +178,7 @@ std::vector<at::Tensor> moe_combine_bwd(const at::Tensor& dout, const at::Tensor
 }
 
 // Zeroes rows of `buf` whose `src` entry is negative (segment padding) in place.
-void moe_zero_padding(at::Tensor& buf, const at::Tensor& src) {
+void moe_zero_padding(at::Tensor& buf, const at::Tensor& src, const c10::optional<at::Tensor>& row_limit) {
   check_cuda_tensor(buf, "buf");
   check_cuda_tensor(src, "src");
   const int64_t rows = src.numel();
@@ -181,7 +186,7 @@ void moe_zero_padding(at::Tensor& buf, const at::Tensor& src) {
   if (rows == 0) return;
   c10::cuda::CUDAGuard guard(buf.device());
   zero_rows_kernel<<<(rows + 7) / 8, 256, 0, stream()>>>(reinterpret_cast<__nv_bfloat16*>(buf.data_ptr()),
-                                                          src.data_ptr<int32_t>(), rows, h);
+                                                          src.data_ptr<int32_t>(), rows, h, limit_ptr(row_limit));
   TDSV_LAUNCH_CHECK();
 }
 

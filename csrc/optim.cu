@@ -16,16 +16,75 @@ namespace tdsv {
 
 namespace {
 
+// Four consecutive elements of T as one vector access (16 B for fp32, 8 B for bf16).
+template <typename T>
+struct Vec4;
+template <>
+struct Vec4<float> {
+  using type = float4;
+  __device__ static void load(const float* p, float (&o)[4]) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
+    o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+  }
+  __device__ static void store(float* p, const float (&o)[4]) {
+    *reinterpret_cast<float4*>(p) = make_float4(o[0], o[1], o[2], o[3]);
+  }
+};
+template <>
+struct Vec4<__nv_bfloat16> {
+  __device__ static void load(const __nv_bfloat16* p, float (&o)[4]) {
+    const uint2 raw = *reinterpret_cast<const uint2*>(p);
+    const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+    const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+    o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
+  }
+  __device__ static void store(__nv_bfloat16* p, const float (&o)[4]) {
+    __nv_bfloat162 a = __floats2bfloat162_rn(o[0], o[1]);
+    __nv_bfloat162 b = __floats2bfloat162_rn(o[2], o[3]);
+    uint2 raw;
+    raw.x = *reinterpret_cast<uint32_t*>(&a);
+    raw.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = raw;
+  }
+};
+
+// Element-wise AdamW; `vectorized` requires 16-byte aligned fp32 and 8-byte aligned bf16 arrays
+// (n is handled with a scalar tail either way).
 template <typename GT, typename MT>
 __global__ void adamw_kernel(float* __restrict__ master, const GT* __restrict__ grad, MT* __restrict__ m,
                              MT* __restrict__ v, __nv_bfloat16* __restrict__ out, int64_t n, float lr, float beta1,
                              float beta2, float eps, float weight_decay, float bc1, float bc2_sqrt,
-                             float grad_scale, const float* __restrict__ grad_scale_ptr) {
+                             float grad_scale, const float* __restrict__ grad_scale_ptr, bool vectorized) {
   const float gs = grad_scale * (grad_scale_ptr != nullptr ? *grad_scale_ptr : 1.f);
   const float step_size = lr / bc1;
   const float decay = 1.f - lr * weight_decay;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  int64_t tail = 0;
+  if (vectorized) {
+    const int64_t n4 = n / 4;
+    for (int64_t q = tid; q < n4; q += stride) {
+      const int64_t i = q * 4;
+      float g[4], p[4], mi[4], vi[4];
+      Vec4<GT>::load(grad + i, g);
+      Vec4<float>::load(master + i, p);
+      Vec4<MT>::load(m + i, mi);
+      Vec4<MT>::load(v + i, vi);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float gk = g[k] * gs;
+        mi[k] = beta1 * mi[k] + (1.f - beta1) * gk;
+        vi[k] = beta2 * vi[k] + (1.f - beta2) * gk * gk;
+        p[k] = p[k] * decay - step_size * mi[k] / (sqrtf(vi[k]) / bc2_sqrt + eps);
+      }
+      Vec4<float>::store(master + i, p);
+      Vec4<MT>::store(m + i, mi);
+      Vec4<MT>::store(v + i, vi);
+      if (out != nullptr) Vec4<__nv_bfloat16>::store(out + i, p);
+    }
+    tail = n4 * 4;
+  }
+  for (int64_t i = tail + tid; i < n; i += stride) {
     const float g = to_float<GT>(grad[i]) * gs;
     float p = master[i] * decay;
     const float mi = beta1 * to_float<MT>(m[i]) + (1.f - beta1) * g;
@@ -97,13 +156,16 @@ void adamw_step(at::Tensor& master, const at::Tensor& grad, at::Tensor& m, at::T
   const float bc1 = static_cast<float>(1.0 - std::pow(beta1, static_cast<double>(step)));
   const float bc2s = static_cast<float>(std::sqrt(1.0 - std::pow(beta2, static_cast<double>(step))));
   c10::cuda::CUDAGuard guard(master.device());
-  const int grid = grid_for(n);
+  const int grid = grid_for((n + 3) / 4);
+  auto aligned = [](const void* p, int bytes) { return reinterpret_cast<uintptr_t>(p) % bytes == 0; };
+  const bool vec = aligned(master.data_ptr(), 16) && aligned(grad.data_ptr(), 16) && aligned(m.data_ptr(), 16) &&
+                   aligned(v.data_ptr(), 16) && (outp == nullptr || aligned(outp, 8));
 #define TDSV_ADAMW(GT, MT, gptr, mptr, vptr)                                                                   \
   adamw_kernel<GT, MT><<<grid, 256, 0, stream()>>>(master.data_ptr<float>(), gptr, mptr, vptr, outp, n,       \
                                                    static_cast<float>(lr), static_cast<float>(beta1),         \
                                                    static_cast<float>(beta2), static_cast<float>(eps),        \
                                                    static_cast<float>(weight_decay), bc1, bc2s,               \
-                                                   static_cast<float>(grad_scale), gsp)
+                                                   static_cast<float>(grad_scale), gsp, vec)
   const bool g32 = grad.scalar_type() == at::kFloat;
   const bool m32 = m.scalar_type() == at::kFloat;
   auto gbf = reinterpret_cast<const __nv_bfloat16*>(grad.data_ptr());

@@ -26,9 +26,9 @@ __device__ __forceinline__ void load_gu(const __nv_bfloat16* gu, int64_t row, in
 
 __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, const float* __restrict__ w,
                                   __nv_bfloat16* __restrict__ out, int64_t rows, int inter, bool interleaved,
-                                  float limit) {
+                                  float limit, const int32_t* __restrict__ row_limit) {
   const int64_t row = blockIdx.x;
-  if (row >= rows) return;
+  if (row >= rows || (row_limit != nullptr && row >= *row_limit)) return;
   const float ws = w != nullptr ? w[row] : 1.f;
   for (int i = threadIdx.x; i < inter; i += blockDim.x) {
     float g, u;
@@ -44,10 +44,11 @@ __global__ void swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu, const fl
 
 __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ gu,
                                   const float* __restrict__ w, __nv_bfloat16* __restrict__ dgu,
-                                  float* __restrict__ dw, int64_t rows, int inter, bool interleaved, float limit) {
+                                  float* __restrict__ dw, int64_t rows, int inter, bool interleaved, float limit,
+                                  const int32_t* __restrict__ row_limit) {
   __shared__ float scratch[32];
   const int64_t row = blockIdx.x;
-  if (row >= rows) return;
+  if (row >= rows || (row_limit != nullptr && row >= *row_limit)) return;
   const float ws = w != nullptr ? w[row] : 1.f;
   float dot = 0.f;
   for (int i = threadIdx.x; i < inter; i += blockDim.x) {
@@ -89,7 +90,12 @@ __global__ void swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const 
 
 }  // namespace
 
-at::Tensor swiglu_fwd(const at::Tensor& gu, const c10::optional<at::Tensor>& w, bool interleaved, double limit) {
+static const int32_t* limit_ptr(const c10::optional<at::Tensor>& t) {
+  return (t.has_value() && t->defined()) ? t->data_ptr<int32_t>() : nullptr;
+}
+
+at::Tensor swiglu_fwd(const at::Tensor& gu, const c10::optional<at::Tensor>& w, bool interleaved, double limit,
+                      const c10::optional<at::Tensor>& row_limit) {
   check_cuda_tensor(gu, "gate_up");
   TDSV_CHECK(gu.scalar_type() == at::kBFloat16 && gu.dim() == 2 && gu.size(1) % 2 == 0, "swiglu: bf16 [R, 2I]");
   const int64_t rows = gu.size(0);
@@ -106,13 +112,14 @@ at::Tensor swiglu_fwd(const at::Tensor& gu, const c10::optional<at::Tensor>& w, 
   const int threads = std::min(1024, std::max(32, ((inter + 31) / 32) * 32 / 2));
   swiglu_fwd_kernel<<<rows, threads, 0, stream()>>>(reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), wp,
                                                     reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, inter,
-                                                    interleaved, static_cast<float>(limit));
+                                                    interleaved, static_cast<float>(limit), limit_ptr(row_limit));
   TDSV_LAUNCH_CHECK();
   return out;
 }
 
 std::vector<at::Tensor> swiglu_bwd(const at::Tensor& dout, const at::Tensor& gu, const c10::optional<at::Tensor>& w,
-                                   bool interleaved, double limit, bool need_dw) {
+                                   bool interleaved, double limit, bool need_dw,
+                                   const c10::optional<at::Tensor>& row_limit) {
   check_cuda_tensor(dout, "dout");
   check_cuda_tensor(gu, "gate_up");
   const int64_t rows = gu.size(0);
@@ -127,7 +134,7 @@ std::vector<at::Tensor> swiglu_bwd(const at::Tensor& dout, const at::Tensor& gu,
   swiglu_bwd_kernel<<<rows, threads, 0, stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), wp,
       reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), need_dw ? dw.data_ptr<float>() : nullptr, rows, inter,
-      interleaved, static_cast<float>(limit));
+      interleaved, static_cast<float>(limit), limit_ptr(row_limit));
   TDSV_LAUNCH_CHECK();
   return {dgu, dw};
 }

@@ -60,7 +60,7 @@ class RoutedExperts(nn.Module):
         row_weights = self.dispatcher.row_weights(batch)
         w1 = self.gate_up.reshape(self.num_experts, 2 * self.intermediate, self.hidden_size)
         gate_up = ops.grouped_linear(batch.rows, w1, batch.offsets, batch.sizes)
-        hidden = ops.swiglu(gate_up, row_weights, interleaved=True, limit=self.limit)
+        hidden = ops.swiglu(gate_up, row_weights, interleaved=True, limit=self.limit, total=batch.total)
         out = ops.grouped_linear(hidden, self.down, batch.offsets, batch.sizes)
         return self.dispatcher.combine(out, batch, weighted=False)
 

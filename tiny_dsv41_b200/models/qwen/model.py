@@ -120,7 +120,7 @@ class Qwen3MoeExperts(nn.Module):
     def forward(self, hidden, selected_experts, weights):
         batch = self.dispatcher.dispatch(hidden, selected_experts, weights)
         gate_up = ops.grouped_linear(batch.rows, self.gate_up_proj, batch.offsets, batch.sizes)
-        act = ops.swiglu(gate_up)
+        act = ops.swiglu(gate_up, total=batch.total)
         out = ops.grouped_linear(act, self.down_proj, batch.offsets, batch.sizes)
         return self.dispatcher.combine(out, batch, weighted=True)
 

@@ -22,9 +22,24 @@ class _LinearCrossEntropy(torch.autograd.Function):
         C = ext()
         rows = hidden.shape[0]
         vocab = weight.shape[0]
-        total = torch.zeros((), dtype=torch.float32, device=hidden.device)
         need_dx = ctx.needs_input_grad[0]
         need_dw = ctx.needs_input_grad[1]
+        if chunk >= rows:
+            # one pass: logits -> in-place CE gradient -> dX and dW GEMMs (bf16 dW, K = all rows)
+            logits = torch.empty(rows, vocab, dtype=torch.bfloat16, device=hidden.device)
+            C.gemm(hidden, weight, logits, False, False, False)
+            loss, _ = C.cross_entropy_fused(logits, targets, 1.0, IGNORE_INDEX, need_dx or need_dw)
+            dx = dw = None
+            if need_dx:
+                dx = torch.empty_like(hidden)
+                C.gemm(logits, weight, dx, False, True, False)
+            if need_dw:
+                dw = torch.empty_like(weight)
+                C.gemm(logits, hidden, dw, True, True, False)
+            ctx.save_for_backward(dx, dw)
+            ctx.weight_dtype = weight.dtype
+            return loss.sum()
+        total = torch.zeros((), dtype=torch.float32, device=hidden.device)
         dx = torch.empty_like(hidden) if need_dx else None
         dw = torch.zeros(weight.shape, dtype=torch.float32, device=hidden.device) if need_dw else None
         for start in range(0, rows, chunk):
@@ -45,14 +60,26 @@ class _LinearCrossEntropy(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad):
         dx, dw = ctx.saved_tensors
-        gdx = None if dx is None else (dx.float() * grad).to(dx.dtype)
-        gdw = None if dw is None else (dw * grad).to(ctx.weight_dtype)
+        gdx = None if dx is None else dx.mul_(grad.to(dx.dtype)) if dx.dtype == torch.float32 else (
+            dx.float() * grad).to(dx.dtype)
+        if dw is None:
+            gdw = None
+        elif dw.dtype == torch.float32:
+            gdw = (dw * grad).to(ctx.weight_dtype)
+        else:
+            gdw = dw.mul_(grad.to(dw.dtype))
         return gdx, gdw, None, None
 
 
 def linear_cross_entropy(hidden: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor,
-                         chunk: int = 1024) -> torch.Tensor:
-    """Sum over rows of CE(hidden @ weight.T, targets) (rows with target -100 are ignored)."""
+                         chunk: int | None = None) -> torch.Tensor:
+    """Sum over rows of CE(hidden @ weight.T, targets) (rows with target -100 are ignored).
+
+    ``chunk`` rows per pass; by default all rows at once when their bf16 logits fit in 4 GiB."""
+    if chunk is None:
+        chunk = hidden.numel() // hidden.shape[-1]
+        if chunk * weight.shape[0] * 2 > 4 * 2 ** 30:
+            chunk = max(128, (4 * 2 ** 30) // (weight.shape[0] * 2) // 128 * 128)
     hidden = hidden.reshape(-1, hidden.shape[-1])
     targets = targets.reshape(-1)
     if on_gpu(hidden) and hidden.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16:

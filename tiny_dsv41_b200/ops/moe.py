@@ -3,8 +3,9 @@
 The routing metadata is built on the device without any host synchronisation (the reference
 pulls split sizes to the host on every layer, ``dsv41_train/dispatch.py:87-89``): each expert's
 routed rows form a segment starting at a multiple of ``BLOCK`` rows; padding rows are zero so
-the grouped GEMMs (``ops.gemm.grouped_linear``) never need masks. The buffer capacity is the
-static upper bound ``T*k + E*(BLOCK-1)``.
+the grouped GEMMs (``ops.gemm.grouped_linear``) never need masks. Buffers have the static
+capacity ``n_routes + E*(BLOCK-1)``; the number of rows actually used is a device scalar
+(``Routing.total``) that the row-wise kernels read to skip the unused tail.
 """
 
 from __future__ import annotations
@@ -21,66 +22,75 @@ BLOCK = 128
 
 @dataclass
 class Routing:
-    route_rows: torch.Tensor   # [T, k] int32 row of each (token, slot) in the expert-major buffer
-    src: torch.Tensor          # [R_cap] int32 source token of each row (-1 = padding)
+    route_rows: torch.Tensor   # [N, k] int32 row of each (item, slot) in the expert-major buffer (-1 = none)
+    src: torch.Tensor          # [R_cap] int32 source item of each row (-1 = padding)
     offsets: torch.Tensor      # [E] int32 segment start rows
     rows: torch.Tensor         # [E] int32 segment sizes (multiples of BLOCK)
     counts: torch.Tensor       # [E] int64 routed rows per expert
+    total: torch.Tensor        # [1] int32 rows in use (sum of segment sizes)
     capacity: int
 
 
 def build_routing(ids: torch.Tensor, num_experts: int, block: int = BLOCK) -> Routing:
-    tokens, k = ids.shape
+    """Expert-major layout for ids [N, k] (entries < 0 are not routed)."""
+    items, k = ids.shape
     flat = ids.reshape(-1).long()
     n = flat.numel()
-    counts = torch.bincount(flat, minlength=num_experts)
+    valid = flat >= 0
+    keyed = torch.where(valid, flat, torch.full_like(flat, num_experts))
+    counts_all = torch.bincount(keyed, minlength=num_experts + 1)
+    counts = counts_all[:num_experts]
     padded = (counts + block - 1) // block * block
     seg_off = torch.cumsum(padded, 0) - padded
-    start = torch.cumsum(counts, 0) - counts
-    order = torch.argsort(flat, stable=True)
-    sorted_e = flat[order]
-    dest = seg_off[sorted_e] + (torch.arange(n, device=ids.device) - start[sorted_e])
+    start = torch.cumsum(counts_all, 0) - counts_all
+    order = torch.argsort(keyed, stable=True)
+    sorted_e = keyed[order]
+    rank_in = torch.arange(n, device=ids.device) - start[sorted_e]
+    seg_off_ext = torch.cat((seg_off, seg_off.new_zeros(1)))
+    dest = torch.where(sorted_e < num_experts, seg_off_ext[sorted_e] + rank_in, torch.full_like(rank_in, -1))
     route_rows = torch.empty(n, dtype=torch.long, device=ids.device)
     route_rows[order] = dest
-    capacity = n + num_experts * (block - 1)
-    capacity = (capacity + block - 1) // block * block
-    src = torch.full((capacity,), -1, dtype=torch.int32, device=ids.device)
-    src[dest] = torch.div(order, k, rounding_mode="floor").to(torch.int32)
-    return Routing(route_rows.view(tokens, k).to(torch.int32), src, seg_off.to(torch.int32),
-                   padded.to(torch.int32), counts, capacity)
+    capacity = (n + num_experts * (block - 1) + block - 1) // block * block
+    src = torch.full((capacity + 1,), -1, dtype=torch.int32, device=ids.device)
+    # invalid routes write into the spare last slot, which is then dropped
+    src[torch.where(dest >= 0, dest, torch.full_like(dest, capacity))] = torch.div(order, k, rounding_mode="floor").to(torch.int32)
+    src = src[:capacity]
+    total = padded.sum().to(torch.int32).reshape(1)
+    return Routing(route_rows.view(items, k).to(torch.int32), src.contiguous(), seg_off.to(torch.int32),
+                   padded.to(torch.int32), counts, total, capacity)
 
 
 class _Gather(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, src, route_rows):
+    def forward(ctx, x, src, route_rows, total):
         ctx.save_for_backward(route_rows)
-        return ext().moe_gather(x.contiguous(), src)
+        return ext().moe_gather(x.contiguous(), src, total)
 
     @staticmethod
     def backward(ctx, drows):
         (route_rows,) = ctx.saved_tensors
-        return ext().moe_combine(drows.contiguous(), route_rows, None), None, None
+        return ext().moe_combine(drows.contiguous(), route_rows, None), None, None, None
 
 
 class _Combine(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, rows, route_rows, weights, src):
-        ctx.save_for_backward(rows, route_rows, weights, src)
+    def forward(ctx, rows, route_rows, weights, src, total):
+        ctx.save_for_backward(rows, route_rows, weights, src, total)
         return ext().moe_combine(rows.contiguous(), route_rows, weights)
 
     @staticmethod
     def backward(ctx, dout):
-        rows, route_rows, weights, src = ctx.saved_tensors
+        rows, route_rows, weights, src, total = ctx.saved_tensors
         need_dw = weights is not None and ctx.needs_input_grad[2]
         drows, dw = ext().moe_combine_bwd(dout.contiguous(), rows, route_rows, weights, need_dw)
-        ext().moe_zero_padding(drows, src)
-        return drows, None, (dw if need_dw else None), None
+        ext().moe_zero_padding(drows, src, total)
+        return drows, None, (dw if need_dw else None), None, None
 
 
 def gather(x: torch.Tensor, routing: Routing) -> torch.Tensor:
-    """[T, H] -> expert-major [R_cap, H] (padding rows zero)."""
+    """[N, H] -> expert-major [R_cap, H] (padding rows zero)."""
     if on_gpu(x):
-        return _Gather.apply(x, routing.src, routing.route_rows)
+        return _Gather.apply(x, routing.src, routing.route_rows, routing.total)
     out = x.new_zeros(routing.capacity, x.shape[-1])
     valid = routing.src >= 0
     out[valid] = x[routing.src[valid].long()]
@@ -91,8 +101,9 @@ def combine(rows: torch.Tensor, routing: Routing, weights: torch.Tensor | None) 
     """sum_slot weights[t, slot] * rows[route_rows[t, slot]] in fp32, fixed slot order."""
     if on_gpu(rows):
         return _Combine.apply(rows, routing.route_rows, None if weights is None else weights.float().contiguous(),
-                              routing.src)
-    picked = rows[routing.route_rows.long()].float()
+                              routing.src, routing.total)
+    index = routing.route_rows.long()
+    picked = rows[index.clamp_min(0)].float() * (index >= 0).unsqueeze(-1)
     if weights is not None:
         picked = picked * weights.float().unsqueeze(-1)
     return picked.sum(1).to(rows.dtype)
@@ -117,24 +128,25 @@ def swiglu_reference(gate_up, weights=None, interleaved=False, limit=0.0):
 
 class _SwiGLU(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, gate_up, weights, interleaved, limit):
-        ctx.save_for_backward(gate_up, weights)
+    def forward(ctx, gate_up, weights, interleaved, limit, total):
+        ctx.save_for_backward(gate_up, weights, total)
         ctx.meta = (interleaved, limit)
-        return ext().swiglu_fwd(gate_up.contiguous(), weights, interleaved, float(limit))
+        return ext().swiglu_fwd(gate_up.contiguous(), weights, interleaved, float(limit), total)
 
     @staticmethod
     def backward(ctx, dout):
-        gate_up, weights = ctx.saved_tensors
+        gate_up, weights, total = ctx.saved_tensors
         interleaved, limit = ctx.meta
         need_dw = weights is not None and ctx.needs_input_grad[1]
-        dgu, dw = ext().swiglu_bwd(dout.contiguous(), gate_up, weights, interleaved, float(limit), need_dw)
-        return dgu, (dw if need_dw else None), None, None
+        dgu, dw = ext().swiglu_bwd(dout.contiguous(), gate_up, weights, interleaved, float(limit), need_dw, total)
+        return dgu, (dw if need_dw else None), None, None, None
 
 
 def swiglu(gate_up: torch.Tensor, weights: torch.Tensor | None = None, *, interleaved: bool = False,
-           limit: float = 0.0) -> torch.Tensor:
-    """silu(gate) * up (optionally clamped, optionally times a per-row weight)."""
+           limit: float = 0.0, total: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(gate) * up (optionally clamped, optionally times a per-row weight). ``total``: optional
+    int32 device scalar; rows at or beyond it are skipped (left undefined)."""
     if on_gpu(gate_up):
         w = None if weights is None else weights.float().contiguous()
-        return _SwiGLU.apply(gate_up, w, interleaved, limit)
+        return _SwiGLU.apply(gate_up, w, interleaved, limit, total)
     return swiglu_reference(gate_up, weights, interleaved, limit)

@@ -36,6 +36,7 @@ class DispatchBatch:
     sizes: torch.Tensor
     row_weights: torch.Tensor | None
     state: dict[str, Any] = field(default_factory=dict)
+    total: torch.Tensor | None = None  # int32 device scalar: rows in use
 
 
 def _row_weights(routing: moe_ops.Routing, weights: torch.Tensor) -> torch.Tensor:
@@ -79,7 +80,7 @@ class TokenDispatcher:
         routing = moe_ops.build_routing(ids, self.num_experts)
         rows = moe_ops.gather(x, routing)
         return DispatchBatch(rows, routing.offsets, routing.rows, None,
-                             {"routing": routing, "weights": weights})
+                             {"routing": routing, "weights": weights}, routing.total)
 
     def row_weights(self, batch: DispatchBatch) -> torch.Tensor:
         routing = batch.state["routing"]
@@ -141,7 +142,7 @@ class AllToAllTokenDispatcher(TokenDispatcher):
         rows = moe_ops.gather(recv_rows, routing)
         state = {"routing": routing, "weights": recv_weights.view(-1, 1), "order": order,
                  "send_splits": send_splits, "recv_splits": recv_splits, "tokens": tokens, "k": k}
-        return DispatchBatch(rows, routing.offsets, routing.rows, None, state)
+        return DispatchBatch(rows, routing.offsets, routing.rows, None, state, routing.total)
 
     def combine(self, y, batch, *, weighted: bool = True):
         s = batch.state

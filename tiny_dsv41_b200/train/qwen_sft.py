@@ -105,6 +105,14 @@ class QwenTrainer:
             fully_shard(layer, ignored_params=ignored, **opts)
         fully_shard(model.lm_head, **opts)
         fully_shard(model, ignored_params=ignored, **opts)
+        # MoE layers issue EP exchanges on their own group in backward; an implicit cross-layer
+        # all-gather prefetch could interleave the two groups' collectives differently on
+        # different ranks, so each FSDP module prefetches nothing but itself.
+        from torch.distributed.fsdp import FSDPModule
+
+        for module in model.modules():
+            if isinstance(module, FSDPModule):
+                module.set_modules_to_backward_prefetch([module])
 
     def train_step(self, input_ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         device = self.runtime.device
