@@ -317,6 +317,13 @@ inline cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
 inline void check_cuda_tensor(const at::Tensor& t, const char* name) {
   TDSV_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
   TDSV_CHECK(t.is_contiguous(), name, " must be contiguous");
+  // a wrapper subclass (e.g. an FSDP2-sharded DTensor used outside its module's forward) has no
+  // storage of the logical shape: refuse it instead of handing a kernel a bad address
+  TDSV_CHECK(t.has_storage() && (t.numel() == 0 || t.data_ptr() != nullptr), name,
+             " has no device storage (a DTensor / sharded parameter?)");
+  TDSV_CHECK(t.numel() == 0 || static_cast<int64_t>(t.storage().nbytes()) >=
+                                   (t.storage_offset() + t.numel()) * static_cast<int64_t>(t.element_size()),
+             name, " is larger than its storage");
 }
 
 }  // namespace tdsv

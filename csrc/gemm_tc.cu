@@ -374,6 +374,7 @@ void bind_primary_context() {
 // Row-major bf16 tensor [outer..., rows, inner] with a box of {64 inner, box_rows rows, 1...}.
 CUtensorMap make_map(const at::Tensor& t, int box_rows) {
   bind_primary_context();
+  check_cuda_tensor(t, "gemm operand");
   TDSV_CHECK(t.scalar_type() == at::kBFloat16, "gemm operands must be bf16");
   TDSV_CHECK(t.is_contiguous(), "gemm operands must be contiguous");
   TDSV_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, "gemm operand base must be 16-byte aligned");

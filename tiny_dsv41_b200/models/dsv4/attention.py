@@ -20,6 +20,7 @@ from torch import nn
 from ... import ops
 from ...ops.sparse_attention import index_scores, sparse_attention
 from ...parallel.cp import ModelContext
+from ..common import Linear
 from .config import DeepSeekV41Config
 
 
@@ -40,8 +41,9 @@ class RotaryEmbedding(nn.Module):
         super().__init__()
         dim = config.qk_rope_head_dim
         self.dim = dim
-        main = 1.0 / (config.rope_theta ** (torch.arange(0, dim, 2).float() / dim))
-        compressed = 1.0 / (config.compress_rope_theta ** (torch.arange(0, dim, 2).float() / dim))
+        # computed on the host even under a meta-device context: these are constants, not weights
+        main = 1.0 / (config.rope_theta ** (torch.arange(0, dim, 2, device="cpu").float() / dim))
+        compressed = 1.0 / (config.compress_rope_theta ** (torch.arange(0, dim, 2, device="cpu").float() / dim))
         scaling = config.rope_scaling or {}
         if scaling.get("rope_type", scaling.get("type")) == "yarn":
             factor = scaling["factor"]
@@ -54,14 +56,19 @@ class RotaryEmbedding(nn.Module):
 
             low = max(math.floor(corrected(beta_fast)), 0)
             high = min(math.ceil(corrected(beta_slow)), dim - 1)
-            ramp = ((torch.arange(dim // 2, dtype=torch.float32) - low) / max(high - low, 1e-3)).clamp(0, 1)
+            ramp = ((torch.arange(dim // 2, dtype=torch.float32, device="cpu") - low) / max(high - low, 1e-3)).clamp(0, 1)
             keep = 1 - ramp
             compressed = compressed / factor * (1 - keep) + compressed * keep
-        self.register_buffer("main", main, persistent=False)
-        self.register_buffer("compressed", compressed, persistent=False)
+        self.register_buffer("main", main.to(torch.empty(0).device), persistent=False)
+        self.register_buffer("compressed", compressed.to(torch.empty(0).device), persistent=False)
+        # fp32 copies outside the buffers: model dtype casts must not round the frequencies
+        self._main_fp32, self._compressed_fp32 = main.clone(), compressed.clone()
+        self._key = (dim, config.rope_theta, config.compress_rope_theta, repr(sorted(scaling.items())))
 
-    def freqs(self, compressed: bool) -> torch.Tensor:
-        return (self.compressed if compressed else self.main).float()
+    def freqs(self, compressed: bool, device=None) -> torch.Tensor:
+        device = self.main.device if device is None else device
+        values = self._compressed_fp32 if compressed else self._main_fp32
+        return ops.rope.cached_freqs(("dsv4", compressed, self._key), values, device)
 
 
 def apply_rope(x: torch.Tensor, positions: torch.Tensor, freqs: torch.Tensor, *, inverse: bool = False) -> torch.Tensor:
@@ -109,8 +116,8 @@ class Compressor(nn.Module):
     def __init__(self, config: DeepSeekV41Config, layer_id: int) -> None:
         super().__init__()
         self.ratio = config.compress_ratios[layer_id]
-        self.kv_proj = nn.Linear(config.hidden_size, config.head_dim, bias=False)
-        self.gate_proj = nn.Linear(config.hidden_size, config.head_dim, bias=False) if self.ratio > 1 else None
+        self.kv_proj = Linear(config.hidden_size, config.head_dim, bias=False)
+        self.gate_proj = Linear(config.hidden_size, config.head_dim, bias=False) if self.ratio > 1 else None
         self.norm = RMSNorm(config.head_dim, config.rms_norm_eps)
 
     def forward(self, x, positions, token_mask, sequence_ids):
@@ -122,7 +129,7 @@ class Compressor(nn.Module):
         complete &= live.gather(1, safe) & sequence_ids.eq(sequence_ids.gather(1, safe))
         group_counts = complete.long().sum(-1)
         if self.gate_proj is None:
-            kv = ops.linear(x, self.kv_proj.weight)
+            kv = self.kv_proj(x)
             gate = None
         else:
             kv = F.linear(x.float(), self.kv_proj.weight.float())
@@ -206,10 +213,10 @@ class SparseIndexer(nn.Module):
         self.block_size = config.candidate_block_size
         self.ratio = config.compress_ratios[layer_id]
         self.rotary = rotary
-        self.q_proj = nn.Linear(config.q_lora_rank, self.num_heads * self.head_dim, bias=False)
-        self.weight_proj = nn.Linear(config.hidden_size, self.num_heads, bias=False)
+        self.q_proj = Linear(config.q_lora_rank, self.num_heads * self.head_dim, bias=False)
+        self.weight_proj = Linear(config.hidden_size, self.num_heads, bias=False)
         if self.owns_keys:
-            self.k_proj = nn.Linear(config.head_dim, self.head_dim, bias=False)
+            self.k_proj = Linear(config.head_dim, self.head_dim, bias=False)
             self.k_norm = RMSNorm(self.head_dim, config.rms_norm_eps)
 
     def forward(self, x, q_residual, latent, group_positions, context: ModelContext, shadow: ShadowIndexers):
@@ -217,7 +224,7 @@ class SparseIndexer(nn.Module):
         if self.owns_keys:
             shadow.index_keys = None
             if latent is not None:
-                keys = self.k_norm(ops.linear(latent, self.k_proj.weight))
+                keys = self.k_norm(self.k_proj(latent))
                 shadow.index_keys = apply_rope(keys, group_positions, self.rotary.freqs(True)).unsqueeze(1)
         if shadow.index_keys is None:
             shadow.topk_indices = None
@@ -235,9 +242,9 @@ class SparseIndexer(nn.Module):
         ends = torch.minimum(seq_ends, starts + visible)
         valid = (context.sequence_ids >= 0) & (starts < ends)
         ends = torch.where(valid, ends, starts)
-        query = ops.linear(q_residual, self.q_proj.weight).view(batch, length, self.num_heads, self.head_dim)
+        query = self.q_proj(q_residual).view(batch, length, self.num_heads, self.head_dim)
         query = apply_rope(query, context.positions, self.rotary.freqs(True))
-        head_weights = ops.linear(x, self.weight_proj.weight).float() * self.num_heads ** -0.5
+        head_weights = self.weight_proj(x).float() * self.num_heads ** -0.5
         width = int((seq_ends - starts).max().item())
         previous = shadow.candidates if self.uses_candidates else None
         scores = index_scores(query, keys, head_weights, starts, ends, width, previous)
@@ -260,31 +267,28 @@ class CSA2Attention(nn.Module):
         self.dropout = config.attention_dropout
         self.ordered_kv_grad = False
         self.rotary = rotary
-        self.q_a = nn.Linear(config.hidden_size, config.q_lora_rank, bias=False)
+        self.q_a = Linear(config.hidden_size, config.q_lora_rank, bias=False)
         self.q_norm = RMSNorm(config.q_lora_rank, config.rms_norm_eps)
-        self.q_b = nn.Linear(config.q_lora_rank, self.num_heads * self.head_dim, bias=False)
-        self.kv_proj = nn.Linear(config.hidden_size, self.head_dim, bias=False)
+        self.q_b = Linear(config.q_lora_rank, self.num_heads * self.head_dim, bias=False)
+        self.kv_proj = Linear(config.hidden_size, self.head_dim, bias=False)
         self.kv_norm = RMSNorm(self.head_dim, config.rms_norm_eps)
         group_input = self.num_heads * self.head_dim // config.o_groups
         self.o_a = GroupedLinear(group_input, config.o_lora_rank, config.o_groups)
-        self.o_b = nn.Linear(config.o_groups * config.o_lora_rank, config.hidden_size, bias=False)
+        self.o_b = Linear(config.o_groups * config.o_lora_rank, config.hidden_size, bias=False)
         self.sinks = AttentionSinks(self.num_heads)
         self.compressor = Compressor(config, layer_id) if layer_id in config.kv_source_layer_ids else None
         self.indexer = SparseIndexer(config, layer_id, rotary) if layer_id in config.index_source_layer_ids else None
         self.mode = (None if self.ratio <= 0 else CSA2Mode.FULL if self.compressor is not None
                      else CSA2Mode.REINDEX if self.indexer is not None else CSA2Mode.REUSE)
 
-    def _q_a(self, x):
-        return ops.linear(x, self.q_a.weight)
-
     def forward(self, x: torch.Tensor, context: ModelContext, shadow: ShadowIndexers) -> torch.Tensor:
         batch, length, _ = x.shape
         compressed = self.ratio > 0
         freqs = self.rotary.freqs(compressed)
-        q_residual = self.q_norm(self._q_a(x))
-        query = ops.linear(q_residual, self.q_b.weight).view(batch, length, self.num_heads, self.head_dim)
+        q_residual = self.q_norm(self.q_a(x))
+        query = self.q_b(q_residual).view(batch, length, self.num_heads, self.head_dim)
         query = apply_rope(query, context.positions, freqs).transpose(1, 2)
-        kv = apply_rope(self.kv_norm(ops.linear(x, self.kv_proj.weight)), context.positions, freqs).unsqueeze(1)
+        kv = apply_rope(self.kv_norm(self.kv_proj(x)), context.positions, freqs).unsqueeze(1)
         kv = context.gather_attention(kv, dim=2)[:, 0]
         entries = topk = None
         if compressed:
@@ -309,7 +313,7 @@ class CSA2Attention(nn.Module):
                                deterministic=self.ordered_kv_grad)
         out = apply_rope(out, context.positions, freqs, inverse=True)
         grouped = out.reshape(batch, length, self.config.o_groups, -1)
-        return ops.linear(self.o_a(grouped).flatten(2), self.o_b.weight)
+        return self.o_b(self.o_a(grouped).flatten(2))
 
 
 __all__ = ["AttentionSinks", "CSA2Attention", "CSA2Mode", "Compressor", "GroupedLinear", "RMSNorm",

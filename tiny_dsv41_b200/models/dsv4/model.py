@@ -33,7 +33,8 @@ from ...ops.router import AuxGradient
 from ...parallel.cp import ContextParallel, ModelContext
 from ...parallel.dispatch import TokenDispatcher
 from ...parallel.engram_offload import CPUEmbeddingLookup
-from .attention import CSA2Attention, GroupedLinear, RMSNorm, RotaryEmbedding, ShadowIndexers
+from ..common import Linear, LMHead
+from .attention import AttentionSinks, CSA2Attention, GroupedLinear, RMSNorm, RotaryEmbedding, ShadowIndexers
 from .config import DeepSeekV41Config
 from .mhc import HyperConnection
 from .moe import RoutedExperts, SparseMoE, TopKRouter
@@ -269,12 +270,12 @@ class Engram(nn.Module):
         self.hidden_size = config.hidden_size
         self.hc_mult = config.hc_mult
         self.eps = config.rms_norm_eps
-        self.proj = nn.Linear(columns * config.engram_head_dim, config.hidden_size * (config.hc_mult + 1), bias=False)
+        self.proj = Linear(columns * config.engram_head_dim, config.hidden_size * (config.hc_mult + 1), bias=False)
         self.q_weight = nn.Parameter(torch.ones(config.hc_mult, config.hidden_size))
         self.k_weight = nn.Parameter(torch.ones(config.hc_mult, config.hidden_size))
 
     def forward(self, streams, rows, mask):
-        key, value = ops.linear(rows.flatten(-2).to(streams.dtype), self.proj.weight).split(
+        key, value = self.proj(rows.flatten(-2).to(streams.dtype)).split(
             [self.hc_mult * self.hidden_size, self.hidden_size], dim=-1)
         key = key.float().unflatten(-1, (self.hc_mult, self.hidden_size))
         hidden = streams.float()
@@ -438,7 +439,7 @@ class DeepSeekV41ForCausalLM(nn.Module):
         self.context_parallel = context_parallel or ContextParallel()
         self.model = DeepSeekV41Model(config, self.context_parallel, token_dispatcher, engram_mesh, layer_ids,
                                       sparse_engram_gradients, engram_offload)
-        self.lm_head = nn.Linear(config.hidden_size, config.vocab_size, bias=False)
+        self.lm_head = LMHead(config.hidden_size, config.vocab_size)
         self.aux_gradient = AuxGradient()
         for module in self.modules():
             if isinstance(module, TopKRouter):
@@ -478,9 +479,22 @@ class DeepSeekV41ForCausalLM(nn.Module):
         self.model.gradient_checkpointing = True
 
     def _token_log_probs(self, hidden, targets, mask, temperature):
-        logits = ops.linear(hidden[mask], self.lm_head.weight).float()
-        selected = ops.token_log_probs(logits, targets[mask], temperature)
+        selected = self.lm_head(hidden[mask], targets[mask], mode="logprob", temperature=temperature)
         return selected.new_zeros(mask.shape).masked_scatter(mask, selected)
+
+    def fp32_island_parameters(self):
+        """mHC mixing parameters and attention sinks stay fp32 under bf16 training."""
+        return [p for m in self.modules() if isinstance(m, (HyperConnection, AttentionSinks))
+                for p in m.parameters(recurse=False)]
+
+    def to_mixed_precision(self, dtype=torch.bfloat16):
+        """Cast to `dtype` except the fp32 islands (and fp32 buffers such as the routing bias)."""
+        islands = {id(p) for p in self.fp32_island_parameters()}
+        for module in self.modules():
+            for name, param in list(module.named_parameters(recurse=False)):
+                if id(param) not in islands and param.is_floating_point():
+                    param.data = param.data.to(dtype)
+        return self
 
     def forward(self, input_ids, attention_mask=None, labels=None, sequence_ids=None, *, target_ids=None,
                 target_mask=None, temperature: float = 1.0, compute_aux_loss: bool = True) -> CausalLMOutput:
@@ -524,11 +538,10 @@ class DeepSeekV41ForCausalLM(nn.Module):
             if sequence_ids is not None:
                 targets[:, :-1].masked_fill_(sequence_ids[:, :-1] != sequence_ids[:, 1:], -100)
             targets = cp.shard(targets).to(hidden.device)
-            loss_sum = ops.linear_cross_entropy(hidden.reshape(-1, hidden.shape[-1]), self.lm_head.weight,
-                                                targets.reshape(-1))
+            loss_sum = self.lm_head(hidden, targets, mode="ce_sum")
             loss = cp.mean_loss(loss_sum, (targets != -100).sum())
         else:
-            logits = ops.linear(hidden, self.lm_head.weight)
+            logits = self.lm_head(hidden)
         if not compute_aux_loss:
             return CausalLMOutput(loss, logits, None, router_logits, token_log_probs)
         local_mask = cp.shard(token_mask)

@@ -15,6 +15,7 @@ from torch import nn
 from ... import ops
 from ...ops.router import AuxGradient
 from ...parallel.dispatch import TokenDispatcher
+from ..common import Linear, fusable
 from .config import DeepSeekV41Config
 
 
@@ -69,15 +70,18 @@ class SharedExpert(nn.Module):
     def __init__(self, config: DeepSeekV41Config) -> None:
         super().__init__()
         inter = config.moe_intermediate_size * config.n_shared_experts
-        self.gate = nn.Linear(config.hidden_size, inter, bias=False)
-        self.up = nn.Linear(config.hidden_size, inter, bias=False)
-        self.down = nn.Linear(inter, config.hidden_size, bias=False)
+        self.gate = Linear(config.hidden_size, inter, bias=False)
+        self.up = Linear(config.hidden_size, inter, bias=False)
+        self.down = Linear(inter, config.hidden_size, bias=False)
         self.limit = config.swiglu_limit
 
     def forward(self, x):
-        gu = ops.linear(x, torch.cat((self.gate.weight, self.up.weight), dim=0))
+        if fusable(self.gate, self.up):
+            gu = ops.linear(x, torch.cat((self.gate.weight, self.up.weight), dim=0))
+        else:
+            gu = torch.cat((self.gate(x), self.up(x)), dim=-1)
         hidden = ops.swiglu(gu.reshape(-1, gu.shape[-1]), limit=self.limit).view(*x.shape[:-1], -1)
-        return ops.linear(hidden.to(x.dtype), self.down.weight)
+        return self.down(hidden.to(x.dtype))
 
 
 class SparseMoE(nn.Module):

@@ -25,6 +25,7 @@ from ... import ops
 from ...ops.router import AuxGradient
 from ...parallel.cp import ContextParallel
 from ...parallel.dispatch import TokenDispatcher
+from ..common import Linear, LMHead, fusable
 from .config import Qwen3MoeConfig
 
 
@@ -50,20 +51,24 @@ class Qwen3MoeAttention(nn.Module):
         self.head_dim = config.head_dim
         self.dropout = config.attention_dropout
         self.eps = config.rms_norm_eps
+        self.rope_theta = config.rope_theta
         bias = config.attention_bias
-        self.q_proj = nn.Linear(config.hidden_size, self.num_heads * self.head_dim, bias=bias)
-        self.k_proj = nn.Linear(config.hidden_size, self.num_key_value_heads * self.head_dim, bias=bias)
-        self.v_proj = nn.Linear(config.hidden_size, self.num_key_value_heads * self.head_dim, bias=bias)
-        self.o_proj = nn.Linear(self.num_heads * self.head_dim, config.hidden_size, bias=bias)
+        self.q_proj = Linear(config.hidden_size, self.num_heads * self.head_dim, bias=bias)
+        self.k_proj = Linear(config.hidden_size, self.num_key_value_heads * self.head_dim, bias=bias)
+        self.v_proj = Linear(config.hidden_size, self.num_key_value_heads * self.head_dim, bias=bias)
+        self.o_proj = Linear(self.num_heads * self.head_dim, config.hidden_size, bias=bias)
         self.q_norm = Qwen3MoeRMSNorm(self.head_dim, config.rms_norm_eps)
         self.k_norm = Qwen3MoeRMSNorm(self.head_dim, config.rms_norm_eps)
 
-    def forward(self, hidden, freqs, position_ids, attention_mask=None):
+    def forward(self, hidden, position_ids, attention_mask=None):
         batch, length, _ = hidden.shape
-        weight = torch.cat((self.q_proj.weight, self.k_proj.weight, self.v_proj.weight), dim=0)
-        qkv = ops.linear(hidden, weight)
-        if self.q_proj.bias is not None:
-            qkv = qkv + torch.cat((self.q_proj.bias, self.k_proj.bias, self.v_proj.bias))
+        freqs = ops.rope.cached_freqs(("rope", self.head_dim, self.rope_theta),
+                                      ops.inv_freq(self.head_dim, self.rope_theta), hidden.device)
+        if fusable(self.q_proj, self.k_proj, self.v_proj):
+            weight = torch.cat((self.q_proj.weight, self.k_proj.weight, self.v_proj.weight), dim=0)
+            qkv = ops.linear(hidden, weight)
+        else:
+            qkv = torch.cat((self.q_proj(hidden), self.k_proj(hidden), self.v_proj(hidden)), dim=-1)
         q, k, v = ops.qk_norm_rope(qkv, self.q_norm.weight, self.k_norm.weight, position_ids, freqs,
                                    self.num_heads, self.num_key_value_heads, self.eps)
         q = q.view(batch, length, self.num_heads, self.head_dim)
@@ -83,23 +88,23 @@ class Qwen3MoeAttention(nn.Module):
             causal = torch.ones(length, length, dtype=torch.bool, device=hidden.device).tril()
             mask = causal.view(1, 1, length, length) & attention_mask.bool()[:, None, None, :]
         out = ops.causal_attention(q, k, v, mask=mask, dropout=self.dropout if self.training else 0.0)
-        out = ops.linear(out.reshape(batch, length, -1), self.o_proj.weight)
-        if self.o_proj.bias is not None:
-            out = out + self.o_proj.bias
-        return out
+        return self.o_proj(out.reshape(batch, length, -1))
 
 
 class Qwen3MoeMLP(nn.Module):
     def __init__(self, config: Qwen3MoeConfig, intermediate_size: int | None = None) -> None:
         super().__init__()
         size = config.intermediate_size if intermediate_size is None else intermediate_size
-        self.gate_proj = nn.Linear(config.hidden_size, size, bias=False)
-        self.up_proj = nn.Linear(config.hidden_size, size, bias=False)
-        self.down_proj = nn.Linear(size, config.hidden_size, bias=False)
+        self.gate_proj = Linear(config.hidden_size, size, bias=False)
+        self.up_proj = Linear(config.hidden_size, size, bias=False)
+        self.down_proj = Linear(size, config.hidden_size, bias=False)
 
     def forward(self, hidden):
-        gu = ops.linear(hidden, torch.cat((self.gate_proj.weight, self.up_proj.weight), dim=0))
-        return ops.linear(ops.swiglu(gu.reshape(-1, gu.shape[-1])).view(*hidden.shape[:-1], -1), self.down_proj.weight)
+        if fusable(self.gate_proj, self.up_proj):
+            gu = ops.linear(hidden, torch.cat((self.gate_proj.weight, self.up_proj.weight), dim=0))
+        else:
+            gu = torch.cat((self.gate_proj(hidden), self.up_proj(hidden)), dim=-1)
+        return self.down_proj(ops.swiglu(gu.reshape(-1, gu.shape[-1])).view(*hidden.shape[:-1], -1))
 
 
 class Qwen3MoeExperts(nn.Module):
@@ -131,7 +136,7 @@ class Qwen3MoeSparseMoeBlock(nn.Module):
         self.num_experts = config.num_experts
         self.top_k = config.num_experts_per_tok
         self.norm_topk_prob = config.norm_topk_prob
-        self.gate = nn.Linear(config.hidden_size, config.num_experts, bias=False)
+        self.gate = Linear(config.hidden_size, config.num_experts, bias=False)
         self.experts = Qwen3MoeExperts(config, dispatcher)
         self.aux: AuxGradient | None = None
         self.stats: list | None = None
@@ -139,7 +144,7 @@ class Qwen3MoeSparseMoeBlock(nn.Module):
     def forward(self, hidden):
         batch, length, size = hidden.shape
         flat = hidden.reshape(-1, size)
-        router_logits = ops.linear(flat, self.gate.weight)
+        router_logits = self.gate(flat)
         selected, weights = ops.route(router_logits, self.top_k, func="softmax", normalize=self.norm_topk_prob,
                                       aux=self.aux)
         if self.stats is not None:
@@ -160,8 +165,8 @@ class Qwen3MoeDecoderLayer(nn.Module):
         self.input_layernorm = Qwen3MoeRMSNorm(config.hidden_size, config.rms_norm_eps)
         self.post_attention_layernorm = Qwen3MoeRMSNorm(config.hidden_size, config.rms_norm_eps)
 
-    def forward(self, hidden, freqs, position_ids, attention_mask=None):
-        hidden = hidden + self.self_attn(self.input_layernorm(hidden), freqs, position_ids, attention_mask)
+    def forward(self, hidden, position_ids, attention_mask=None):
+        hidden = hidden + self.self_attn(self.input_layernorm(hidden), position_ids, attention_mask)
         out = self.mlp(self.post_attention_layernorm(hidden))
         logits = None
         if isinstance(out, tuple):
@@ -186,7 +191,6 @@ class Qwen3MoeModel(nn.Module):
                                     for i in range(config.num_hidden_layers))
         self.norm = Qwen3MoeRMSNorm(config.hidden_size, config.rms_norm_eps)
         self.gradient_checkpointing = False
-        self.register_buffer("rope_inv_freq", ops.inv_freq(config.head_dim, config.rope_theta), persistent=False)
 
     def forward(self, input_ids, attention_mask=None, position_ids=None, *, output_router_logits=False):
         if input_ids.ndim != 2:
@@ -202,13 +206,12 @@ class Qwen3MoeModel(nn.Module):
         if attention_mask is not None:
             attention_mask = cp.shard(attention_mask)
         hidden = self.embed_tokens(input_ids)
-        freqs = self.rope_inv_freq.float()
         collected = []
         for layer in self.layers:
             if self.gradient_checkpointing and self.training and torch.is_grad_enabled():
-                hidden, logits = checkpoint(layer, hidden, freqs, position_ids, attention_mask, use_reentrant=False)
+                hidden, logits = checkpoint(layer, hidden, position_ids, attention_mask, use_reentrant=False)
             else:
-                hidden, logits = layer(hidden, freqs, position_ids, attention_mask)
+                hidden, logits = layer(hidden, position_ids, attention_mask)
             if output_router_logits and logits is not None:
                 collected.append(logits)
         return Qwen3MoeModelOutput(self.norm(hidden), tuple(collected) if output_router_logits else None)
@@ -228,7 +231,7 @@ class Qwen3MoeForCausalLM(nn.Module):
         self.config = config
         self.context_parallel = context_parallel or ContextParallel()
         self.model = Qwen3MoeModel(config, self.context_parallel, token_dispatcher)
-        self.lm_head = nn.Linear(config.hidden_size, config.vocab_size, bias=False)
+        self.lm_head = LMHead(config.hidden_size, config.vocab_size)
         self.aux_gradient = AuxGradient()
         for module in self.modules():
             if isinstance(module, Qwen3MoeSparseMoeBlock):
@@ -279,13 +282,12 @@ class Qwen3MoeForCausalLM(nn.Module):
             if attention_mask is not None:
                 targets[:, :-1].masked_fill_(~attention_mask[:, 1:].bool(), -100)
             targets = cp.shard(targets)
-            loss_sum = ops.linear_cross_entropy(hidden.reshape(-1, hidden.shape[-1]), self.lm_head.weight,
-                                                targets.reshape(-1))
+            loss_sum = self.lm_head(hidden, targets, mode="ce_sum")
             loss = cp.mean_loss(loss_sum, (targets != -100).sum())
             if aux_loss is not None:
                 loss = loss + self.config.router_aux_loss_coef * aux_loss.detach()
         else:
-            logits = ops.linear(hidden, self.lm_head.weight)
+            logits = self.lm_head(hidden)
         return Qwen3MoeCausalLMOutput(loss, logits, aux_loss, output.router_logits)
 
     def _aux_loss(self, stats, attention_mask):

@@ -7,6 +7,7 @@ from .gemm import grouped_linear, linear, matmul_nt
 from .loss import linear_cross_entropy, token_log_probs
 from .moe import Routing, build_routing, combine, gather, swiglu
 from .norm import rms_norm
+from . import rope
 from .rope import inv_freq, qk_norm_rope, rope_interleaved
 from .router import AuxGradient, route
 

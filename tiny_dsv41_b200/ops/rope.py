@@ -18,6 +18,21 @@ def inv_freq(dim: int, theta: float, device=None) -> torch.Tensor:
     return 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float32, device=device) / dim))
 
 
+_FREQ_CACHE: dict = {}
+
+
+def cached_freqs(key, values: torch.Tensor, device) -> torch.Tensor:
+    """fp32 frequency table on `device`, kept outside module buffers so that dtype casts of the
+    model (``.to(bfloat16)``, FSDP mixed-precision input casts) never touch it."""
+    device = torch.device(device)
+    full = (key, str(device))
+    table = _FREQ_CACHE.get(full)
+    if table is None:
+        table = values.detach().to(device=device, dtype=torch.float32).contiguous()
+        _FREQ_CACHE[full] = table
+    return table
+
+
 def _rotate_half(x: torch.Tensor) -> torch.Tensor:
     first, second = x.chunk(2, dim=-1)
     return torch.cat((-second, first), dim=-1)

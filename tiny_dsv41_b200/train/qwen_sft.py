@@ -62,10 +62,6 @@ class QwenTrainer:
         with torch.device("meta"):
             model = Qwen3MoeForCausalLM(config, cp, token_dispatcher)
         model = model.to_empty(device=rt.device).to(torch.bfloat16)
-        model.model.rope_inv_freq = model.model.rope_inv_freq.float()
-        from ..ops.rope import inv_freq
-
-        model.model.rope_inv_freq = inv_freq(config.head_dim, config.rope_theta, rt.device)
         _init_on_device(model, seed, rt.rank)
         if gradient_checkpointing:
             model.gradient_checkpointing_enable()
@@ -104,7 +100,9 @@ class QwenTrainer:
         for layer in model.model.layers:
             fully_shard(layer, ignored_params=ignored, **opts)
         fully_shard(model.lm_head, **opts)
-        fully_shard(model, ignored_params=ignored, **opts)
+        # the root keeps its parameters gathered between forward and backward (FSDP2's default
+        # for a root): its output is a dataclass, so no pre-backward hook could re-gather them
+        fully_shard(model, mesh=mesh, mp_policy=policy, ignored_params=ignored)
         # MoE layers issue EP exchanges on their own group in backward; an implicit cross-layer
         # all-gather prefetch could interleave the two groups' collectives differently on
         # different ranks, so each FSDP module prefetches nothing but itself.
