@@ -34,7 +34,7 @@ namespace {
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle atom row
 constexpr int kThreads = 192;
-constexpr int kMaxGroups = 1024;
+constexpr int kMaxGroups = 512;
 
 enum Mode : int { kDense = 0, kGroupM = 1, kGroupK = 2 };
 enum Epi : int { kStoreBF16 = 0, kStoreF32 = 1, kAccumF32 = 2 };
@@ -51,12 +51,14 @@ struct Params {
   int* status;
 };
 
+constexpr int kStageC = 32 * 128;  // one warp's epilogue chunk: 32 rows x 128 bytes
+
 template <int BN>
 struct Smem {
   static constexpr int kStageA = BM * BK * 2;
   static constexpr int kStageB = BN * BK * 2;
   static constexpr int kStages = BN == 256 ? 4 : 6;
-  static constexpr int kBytes = kStages * (kStageA + kStageB) + 1024 /*align*/ + 512 /*barriers*/ +
+  static constexpr int kBytes = kStages * (kStageA + kStageB) + 4 * kStageC + 1024 /*align*/ + 512 /*barriers*/ +
                                 kMaxGroups * 4 /*group tile prefix*/;
 };
 
@@ -128,14 +130,15 @@ __device__ __forceinline__ bool tile_info(const Params& p, const int* prefix, in
 template <bool A_MN, bool B_MN, int BN, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tma_a, const __grid_constant__ CUtensorMap tma_b,
-                   const Params p) {
+                   const __grid_constant__ CUtensorMap tma_c, const Params p) {
   using S = Smem<BN>;
   constexpr int kStages = S::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem;
   uint8_t* smem_b = smem + kStages * S::kStageA;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem_b + kStages * S::kStageB);
+  uint8_t* smem_c = smem_b + kStages * S::kStageB;  // 4 x kStageC epilogue staging (1024-aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_c + 4 * kStageC);
   uint64_t* empty = full + kStages;
   uint64_t* tfull = empty + kStages;   // [2]
   uint64_t* tempty = tfull + 2;        // [2]
@@ -261,7 +264,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5)
+    // Each warp drains its 32 TMEM lanes in chunks of 128-byte rows (64 bf16 or 32 fp32 columns),
+    // writes them 128B-swizzled into its own shared staging buffer and issues one TMA store (or
+    // TMA reduce-add for accumulation) per chunk; the TMA clips rows/columns outside the output.
     const int quarter = warp & 3;  // TMEM lanes this warp may access
+    uint8_t* stage = smem_c + quarter * kStageC;
+    const uint32_t stage_u32 = smem_u32(stage);
+    const bool bf16_out = p.epi == kStoreBF16;
+    const int cols_per_chunk = bf16_out ? 64 : 32;
     uint32_t tcount = 0;
     TileInfo ti;
     for (int tile = blockIdx.x; tile_info<MODE, BN>(p, prefix, total_tiles, tile, ti);
@@ -270,67 +280,59 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tph = (tcount >> 1) & 1;
       if (!mbar_wait(&tfull[buf], tph, p.status, kTimeoutAccum)) { *aborted = 1; break; }
       tc_fence_after();
-      const int row = ti.m0 + quarter * 32 + lane;
-      const bool row_ok = row < ti.m_limit;
       const bool zero = ti.k_len <= 0;
       const uint32_t t_addr = tmem_base + buf * BN + (static_cast<uint32_t>(quarter * 32) << 16);
-      int64_t c_row;
-      if (MODE == kGroupK) c_row = static_cast<int64_t>(ti.group) * p.group_stride_c + static_cast<int64_t>(row) * p.ldc;
-      else c_row = static_cast<int64_t>(row) * p.ldc;
+      const int row0 = ti.m0 + quarter * 32;
 #pragma unroll 1
-      for (int j = 0; j < BN / 32; ++j) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_addr + j * 32, r);
+      for (int c0 = 0; c0 < BN; c0 += cols_per_chunk) {
+        uint32_t r[64];
+        tmem_ld_32x32b_x32(t_addr + c0, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+        if (bf16_out) tmem_ld_32x32b_x32(t_addr + c0 + 32, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
         tmem_ld_wait();
-        const int col0 = ti.n0 + j * 32;
-        if (!row_ok || col0 >= p.N) continue;
-        const int ncols = min(32, p.N - col0);
-        if (p.epi == kStoreBF16) {
-          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + c_row + col0;
-          if (ncols == 32) {
+        // the previous chunk's TMA must have finished reading the staging buffer
+        if (lane == 0) bulk_wait_group_read0();
+        __syncwarp();
+        uint8_t* my_row = stage + lane * 128;
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              bf16x8 pack;
+        for (int g = 0; g < 8; ++g) {
+          uint4 v;
+          if (bf16_out) {
+            __nv_bfloat162 h[4];
 #pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const float a = zero ? 0.f : __uint_as_float(r[v * 8 + 2 * i]);
-                const float b = zero ? 0.f : __uint_as_float(r[v * 8 + 2 * i + 1]);
-                pack.v[i] = __floats2bfloat162_rn(a, b);
-              }
-              reinterpret_cast<bf16x8*>(dst)[v] = pack;
+            for (int i = 0; i < 4; ++i) {
+              const float a = zero ? 0.f : __uint_as_float(r[g * 8 + 2 * i]);
+              const float b = zero ? 0.f : __uint_as_float(r[g * 8 + 2 * i + 1]);
+              h[i] = __floats2bfloat162_rn(a, b);
             }
+            v = *reinterpret_cast<uint4*>(h);
           } else {
-            for (int i = 0; i < ncols; ++i) dst[i] = f2bf(zero ? 0.f : __uint_as_float(r[i]));
+            v.x = zero ? 0u : r[g * 4 + 0];
+            v.y = zero ? 0u : r[g * 4 + 1];
+            v.z = zero ? 0u : r[g * 4 + 2];
+            v.w = zero ? 0u : r[g * 4 + 3];
           }
-        } else {
-          float* dst = reinterpret_cast<float*>(p.C) + c_row + col0;
-          const bool acc = p.epi == kAccumF32;
-          if (ncols == 32) {
-#pragma unroll
-            for (int v = 0; v < 8; ++v) {
-              float4 o;
-              o.x = zero ? 0.f : __uint_as_float(r[v * 4 + 0]);
-              o.y = zero ? 0.f : __uint_as_float(r[v * 4 + 1]);
-              o.z = zero ? 0.f : __uint_as_float(r[v * 4 + 2]);
-              o.w = zero ? 0.f : __uint_as_float(r[v * 4 + 3]);
-              if (acc) {
-                const float4 old = reinterpret_cast<const float4*>(dst)[v];
-                o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
-              }
-              reinterpret_cast<float4*>(dst)[v] = o;
-            }
+          *reinterpret_cast<uint4*>(my_row + ((g ^ (lane & 7)) << 4)) = v;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && ti.n0 + c0 < p.N && row0 < ti.m_limit) {
+          const int x = ti.n0 + c0;
+          if (MODE == kGroupK) {
+            if (p.epi == kAccumF32) tma_reduce_add_3d(&tma_c, stage_u32, x, row0, ti.group);
+            else tma_store_3d(&tma_c, stage_u32, x, row0, ti.group);
           } else {
-            for (int i = 0; i < ncols; ++i) {
-              const float val = zero ? 0.f : __uint_as_float(r[i]);
-              dst[i] = acc ? dst[i] + val : val;
-            }
+            if (p.epi == kAccumF32) tma_reduce_add_2d(&tma_c, stage_u32, x, row0);
+            else tma_store_2d(&tma_c, stage_u32, x, row0);
           }
+          bulk_commit_group();
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[buf]);
     }
+    if (lane == 0) bulk_wait_group0();
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -371,37 +373,44 @@ void bind_primary_context() {
   }
 }
 
-// Row-major bf16 tensor [outer..., rows, inner] with a box of {64 inner, box_rows rows, 1...}.
-CUtensorMap make_map(const at::Tensor& t, int box_rows) {
+// Row-major tensor [outer..., rows, inner] with a box of {box_inner, box_rows, 1...}, 128B swizzle.
+CUtensorMap make_map(const at::Tensor& t, int box_rows, int box_inner = 64) {
   bind_primary_context();
   check_cuda_tensor(t, "gemm operand");
-  TDSV_CHECK(t.scalar_type() == at::kBFloat16, "gemm operands must be bf16");
-  TDSV_CHECK(t.is_contiguous(), "gemm operands must be contiguous");
-  TDSV_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, "gemm operand base must be 16-byte aligned");
+  const bool bf16 = t.scalar_type() == at::kBFloat16;
+  TDSV_CHECK(bf16 || t.scalar_type() == at::kFloat, "gemm tensors must be bf16 (operands) or fp32 (outputs)");
+  const int esize = bf16 ? 2 : 4;
+  TDSV_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, "gemm tensor base must be 16-byte aligned");
   const int rank = static_cast<int>(t.dim());
-  TDSV_CHECK(rank == 2 || rank == 3, "gemm operands must be 2-D or 3-D");
+  TDSV_CHECK(rank == 2 || rank == 3, "gemm tensors must be 2-D or 3-D");
   cuuint64_t dims[3];
   cuuint64_t strides[2];
-  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_rows), 1};
+  cuuint32_t box[3] = {static_cast<cuuint32_t>(box_inner), static_cast<cuuint32_t>(box_rows), 1};
   cuuint32_t estr[3] = {1, 1, 1};
   dims[0] = static_cast<cuuint64_t>(t.size(rank - 1));
   dims[1] = static_cast<cuuint64_t>(t.size(rank - 2));
-  TDSV_CHECK((dims[0] * 2) % 16 == 0, "gemm inner dimension must be a multiple of 8 elements");
-  strides[0] = dims[0] * 2;
+  TDSV_CHECK((dims[0] * esize) % 16 == 0, "gemm inner dimension must be a multiple of 16 bytes");
+  strides[0] = dims[0] * esize;
   if (rank == 3) {
     dims[2] = static_cast<cuuint64_t>(t.size(0));
-    strides[1] = dims[0] * dims[1] * 2;
+    strides[1] = dims[0] * dims[1] * esize;
   }
   CUtensorMap map;
-  CUresult r = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, t.data_ptr(), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = encode_fn()(&map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, rank,
+                           t.data_ptr(), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", static_cast<int>(r));
   return map;
 }
 
+// Output map: 32-row boxes of 128 bytes (64 bf16 or 32 fp32 columns).
+CUtensorMap make_out_map(const at::Tensor& out) {
+  return make_map(out, 32, out.scalar_type() == at::kBFloat16 ? 64 : 32);
+}
+
 template <bool A_MN, bool B_MN, int BN, int MODE>
-void launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int max_tiles) {
+void launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const Params& p, int max_tiles) {
   using S = Smem<BN>;
   auto kern = gemm_tc_kernel<A_MN, B_MN, BN, MODE>;
   static bool configured = false;
@@ -416,27 +425,38 @@ void launch(const CUtensorMap& ma, const CUtensorMap& mb, const Params& p, int m
   const int grid = std::max(1, std::min(num_sms(), max_tiles));
   // Launch through an argument array that points at our own 64-byte aligned tensor maps rather
   // than through the <<<>>> stub, which passes the over-aligned CUtensorMap by value.
-  void* args[] = {const_cast<CUtensorMap*>(&ma), const_cast<CUtensorMap*>(&mb), const_cast<Params*>(&p)};
+  void* args[] = {const_cast<CUtensorMap*>(&ma), const_cast<CUtensorMap*>(&mb), const_cast<CUtensorMap*>(&mc),
+                  const_cast<Params*>(&p)};
   TDSV_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(kThreads), args,
                                    S::kBytes, stream()));
 }
 
 template <int MODE>
-void dispatch(bool a_mn, bool b_mn, int bn, const CUtensorMap& ma, const CUtensorMap& mb, const Params& p,
-              int max_tiles) {
+void dispatch(bool a_mn, bool b_mn, int bn, const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc,
+              const Params& p, int max_tiles) {
 #define TDSV_GEMM_CASE(AM, BMN, BNV)                                        \
   if (a_mn == AM && b_mn == BMN && bn == BNV) {                             \
-    launch<AM, BMN, BNV, MODE>(ma, mb, p, max_tiles);                       \
+    launch<AM, BMN, BNV, MODE>(ma, mb, mc, p, max_tiles);                   \
     return;                                                                 \
   }
-  TDSV_GEMM_CASE(false, false, 256)
-  TDSV_GEMM_CASE(false, false, 128)
-  TDSV_GEMM_CASE(false, true, 256)
-  TDSV_GEMM_CASE(false, true, 128)
-  TDSV_GEMM_CASE(true, true, 256)
-  TDSV_GEMM_CASE(true, true, 128)
-  TDSV_GEMM_CASE(true, false, 256)
-  TDSV_GEMM_CASE(true, false, 128)
+  if constexpr (MODE == kDense) {
+    TDSV_GEMM_CASE(false, false, 256)
+    TDSV_GEMM_CASE(false, false, 128)
+    TDSV_GEMM_CASE(false, true, 256)
+    TDSV_GEMM_CASE(false, true, 128)
+    TDSV_GEMM_CASE(true, true, 256)
+    TDSV_GEMM_CASE(true, true, 128)
+    TDSV_GEMM_CASE(true, false, 256)
+    TDSV_GEMM_CASE(true, false, 128)
+  } else if constexpr (MODE == kGroupM) {
+    TDSV_GEMM_CASE(false, false, 256)
+    TDSV_GEMM_CASE(false, false, 128)
+    TDSV_GEMM_CASE(false, true, 256)
+    TDSV_GEMM_CASE(false, true, 128)
+  } else {
+    TDSV_GEMM_CASE(true, true, 256)
+    TDSV_GEMM_CASE(true, true, 128)
+  }
 #undef TDSV_GEMM_CASE
   TORCH_CHECK(false, "unsupported gemm configuration");
 }
@@ -470,6 +490,7 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, 
   const int bn = N >= 256 ? 256 : 128;
   const CUtensorMap ma = make_map(a, a_mn ? BK : BM);
   const CUtensorMap mb = make_map(b, b_mn ? BK : bn);
+  const CUtensorMap mc = make_out_map(out);
   Params p{};
   p.M = M;
   p.N = N;
@@ -484,7 +505,7 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, 
     return;
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
-  dispatch<kDense>(a_mn, b_mn, bn, ma, mb, p, tiles);
+  dispatch<kDense>(a_mn, b_mn, bn, ma, mb, mc, p, tiles);
 }
 
 // Expert-grouped along M: out[off_g : off_g + rows_g] = A[off_g : ...] * B[g]^T.
@@ -509,6 +530,7 @@ void grouped_gemm_m(const at::Tensor& a, const at::Tensor& b, const at::Tensor& 
   const int bn = N >= 256 ? 256 : 128;
   const CUtensorMap ma = make_map(a, BM);
   const CUtensorMap mb = make_map(b, b_mn ? BK : bn);
+  const CUtensorMap mc = make_out_map(out);
   Params p{};
   p.M = static_cast<int>(a.size(0));
   p.N = N;
@@ -522,7 +544,7 @@ void grouped_gemm_m(const at::Tensor& a, const at::Tensor& b, const at::Tensor& 
   p.status = status_word_ptr();
   const int64_t rows = max_rows > 0 ? max_rows : a.size(0);
   const int max_tiles = static_cast<int>(((rows + BM - 1) / BM) * ((N + bn - 1) / bn));
-  dispatch<kGroupM>(false, b_mn, bn, ma, mb, p, max_tiles);
+  dispatch<kGroupM>(false, b_mn, bn, ma, mb, mc, p, max_tiles);
 }
 
 // Expert-grouped along K (weight gradients): out[g] = A_g^T * B_g with A_g = a[off_g : off_g + rows_g]
@@ -546,6 +568,7 @@ void grouped_gemm_k(const at::Tensor& a, const at::Tensor& b, const at::Tensor& 
   const int bn = N >= 256 ? 256 : 128;
   const CUtensorMap ma = make_map(a, BK);
   const CUtensorMap mb = make_map(b, BK);
+  const CUtensorMap mc = make_out_map(out);
   Params p{};
   p.M = M;
   p.N = N;
@@ -559,7 +582,7 @@ void grouped_gemm_k(const at::Tensor& a, const at::Tensor& b, const at::Tensor& 
   p.epi = epi_code(out, accumulate);
   p.status = status_word_ptr();
   const int tiles = G * ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
-  dispatch<kGroupK>(true, true, bn, ma, mb, p, tiles);
+  dispatch<kGroupK>(true, true, bn, ma, mb, mc, p, tiles);
 }
 
 }  // namespace tdsv
