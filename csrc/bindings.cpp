@@ -34,6 +34,9 @@ namespace tdsv {
 // status
 int64_t read_status();
 // norm.cu
+std::vector<at::Tensor> moe_route_plan(const at::Tensor& ids, int64_t num_experts, int64_t block,
+                                       const c10::optional<at::Tensor>& slab_counts, int64_t slab);
+std::vector<at::Tensor> ep_dest_plan(const at::Tensor& ids, int64_t experts_per_rank, int64_t ranks);
 std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, double eps);
 std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
                                     const at::Tensor& rstd, bool need_dw);
@@ -115,6 +118,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "tiny_dsv41_b200 sm_100a kernels";
   maybe_install_segv_handler();
   m.def("read_status", &tdsv::read_status, "read and clear the device pipeline status word");
+  m.def("moe_route_plan", &tdsv::moe_route_plan, "expert-major routing plan (stable, 128-row segments)",
+        py::arg("ids"), py::arg("num_experts"), py::arg("block") = 128, py::arg("slab_counts") = py::none(),
+        py::arg("slab") = 1);
+  m.def("ep_dest_plan", &tdsv::ep_dest_plan, "per-token destination ranks, receive slots and counts");
   m.def("rmsnorm_fwd", &tdsv::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &tdsv::rmsnorm_bwd);
   m.def("column_sum", &tdsv::column_sum);

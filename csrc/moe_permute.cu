@@ -19,31 +19,35 @@ namespace {
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, const int32_t* __restrict__ src,
                                    __nv_bfloat16* __restrict__ out, int64_t rows, int h,
                                    const int32_t* __restrict__ row_limit) {
-  // one warp per row, 16B vectors
+  // one warp per row, 16B vectors, grid-stride over the live rows
   const int lane = threadIdx.x & 31;
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (r >= rows || (row_limit != nullptr && r >= *row_limit)) return;
-  const int s = src[r];
+  const int64_t live = row_limit != nullptr ? min(rows, static_cast<int64_t>(*row_limit)) : rows;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   const int vecs = h / 8;
-  bf16x8* dst = reinterpret_cast<bf16x8*>(out + r * h);
-  if (s < 0) {
-    bf16x8 z;
+  bf16x8 z;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) z.v[i] = __floats2bfloat162_rn(0.f, 0.f);
-    for (int v = lane; v < vecs; v += 32) dst[v] = z;
-    return;
+  for (int i = 0; i < 4; ++i) z.v[i] = __floats2bfloat162_rn(0.f, 0.f);
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < live; r += warps) {
+    const int s = src[r];
+    bf16x8* dst = reinterpret_cast<bf16x8*>(out + r * h);
+    if (s < 0) {
+      for (int v = lane; v < vecs; v += 32) dst[v] = z;
+      continue;
+    }
+    const bf16x8* sp = reinterpret_cast<const bf16x8*>(x + static_cast<int64_t>(s) * h);
+    for (int v = lane; v < vecs; v += 32) dst[v] = sp[v];
   }
-  const bf16x8* sp = reinterpret_cast<const bf16x8*>(x + static_cast<int64_t>(s) * h);
-  for (int v = lane; v < vecs; v += 32) dst[v] = sp[v];
 }
 
-// One block per token; each thread owns 8 columns per pass.
+// One warp per token (grid-stride); each lane owns 8 columns per pass.
 __global__ void combine_rows_kernel(const __nv_bfloat16* __restrict__ rows, const int32_t* __restrict__ idx,
                                     const float* __restrict__ w, __nv_bfloat16* __restrict__ out, int64_t tokens,
                                     int k, int h) {
-  const int64_t t = blockIdx.x;
-  if (t >= tokens) return;
-  for (int c = threadIdx.x * 8; c < h; c += blockDim.x * 8) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < tokens;
+       t += warps)
+  for (int c = lane * 8; c < h; c += 256) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int s = 0; s < k; ++s) {
       const int r = idx[t * k + s];
@@ -59,19 +63,21 @@ __global__ void combine_rows_kernel(const __nv_bfloat16* __restrict__ rows, cons
 }
 
 // Backward of combine: scatter weighted dout into the row buffer and compute dweights.
+// One warp per token (grid-stride); unrouted slots cost one index read.
 __global__ void combine_rows_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ rows,
                                         const int32_t* __restrict__ idx, const float* __restrict__ w,
                                         __nv_bfloat16* __restrict__ drows, float* __restrict__ dw, int64_t tokens,
                                         int k, int h) {
-  __shared__ float scratch[32];
-  const int64_t t = blockIdx.x;
-  if (t >= tokens) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < tokens;
+       t += warps)
   for (int s = 0; s < k; ++s) {
     const int r = idx[t * k + s];
     float dot = 0.f;
     if (r >= 0) {
       const float ws = w != nullptr ? w[t * k + s] : 1.f;
-      for (int c = threadIdx.x * 8; c < h; c += blockDim.x * 8) {
+      for (int c = lane * 8; c < h; c += 256) {
         float g[8], v[8], o[8];
         load_bf16x8(dout + t * h + c, g);
         if (dw != nullptr) {
@@ -84,9 +90,9 @@ __global__ void combine_rows_bwd_kernel(const __nv_bfloat16* __restrict__ dout, 
         store_bf16x8(drows + static_cast<int64_t>(r) * h + c, o);
       }
     }
-    if (dw != nullptr) {
-      dot = block_sum(dot, scratch);
-      if (threadIdx.x == 0) dw[t * k + s] = r >= 0 ? dot : 0.f;
+    if (dw != nullptr && r >= 0) {
+      dot = warp_sum(dot);
+      if (lane == 0) dw[t * k + s] = dot;
     }
   }
 }
@@ -95,16 +101,25 @@ __global__ void combine_rows_bwd_kernel(const __nv_bfloat16* __restrict__ dout, 
 __global__ void zero_rows_kernel(__nv_bfloat16* __restrict__ buf, const int32_t* __restrict__ src, int64_t rows,
                                  int h, const int32_t* __restrict__ row_limit) {
   const int lane = threadIdx.x & 31;
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (r >= rows || (row_limit != nullptr && r >= *row_limit) || src[r] >= 0) return;
+  const int64_t live = row_limit != nullptr ? min(rows, static_cast<int64_t>(*row_limit)) : rows;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   bf16x8 z;
 #pragma unroll
   for (int i = 0; i < 4; ++i) z.v[i] = __floats2bfloat162_rn(0.f, 0.f);
-  bf16x8* dst = reinterpret_cast<bf16x8*>(buf + r * h);
-  for (int v = lane; v < h / 8; v += 32) dst[v] = z;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < live; r += warps) {
+    if (src[r] >= 0) continue;
+    bf16x8* dst = reinterpret_cast<bf16x8*>(buf + r * h);
+    for (int v = lane; v < h / 8; v += 32) dst[v] = z;
+  }
 }
 
 }  // namespace
+
+// Blocks of 8 warps for `items` warp-sized work items, at most 8 blocks per SM (grid-stride).
+static int warp_grid(int64_t items) {
+  const int64_t want = (items + 7) / 8;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(num_sms()) * 8)));
+}
 
 static const int32_t* limit_ptr(const c10::optional<at::Tensor>& t) {
   return (t.has_value() && t->defined()) ? t->data_ptr<int32_t>() : nullptr;
@@ -121,7 +136,7 @@ at::Tensor moe_gather(const at::Tensor& x, const at::Tensor& src, const c10::opt
   auto out = at::empty({rows, h}, x.options());
   if (rows == 0) return out;
   c10::cuda::CUDAGuard guard(x.device());
-  gather_rows_kernel<<<(rows + 7) / 8, 256, 0, stream()>>>(
+  gather_rows_kernel<<<warp_grid(rows), 256, 0, stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), src.data_ptr<int32_t>(),
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, h, limit_ptr(row_limit));
   TDSV_LAUNCH_CHECK();
@@ -145,8 +160,7 @@ at::Tensor moe_combine(const at::Tensor& rows, const at::Tensor& idx, const c10:
     wp = w->data_ptr<float>();
   }
   c10::cuda::CUDAGuard guard(rows.device());
-  const int threads = std::min(256, std::max(32, h / 8));
-  combine_rows_kernel<<<tokens, threads, 0, stream()>>>(reinterpret_cast<const __nv_bfloat16*>(rows.data_ptr()),
+  combine_rows_kernel<<<warp_grid(tokens), 256, 0, stream()>>>(reinterpret_cast<const __nv_bfloat16*>(rows.data_ptr()),
                                                         idx.data_ptr<int32_t>(), wp,
                                                         reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), tokens, k, h);
   TDSV_LAUNCH_CHECK();
@@ -167,8 +181,7 @@ std::vector<at::Tensor> moe_combine_bwd(const at::Tensor& dout, const at::Tensor
   if (w.has_value() && w->defined()) wp = w->data_ptr<float>();
   c10::cuda::CUDAGuard guard(rows.device());
   if (tokens > 0) {
-    const int threads = std::min(256, std::max(32, h / 8));
-    combine_rows_bwd_kernel<<<tokens, threads, 0, stream()>>>(
+    combine_rows_bwd_kernel<<<warp_grid(tokens), 256, 0, stream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(rows.data_ptr()),
         idx.data_ptr<int32_t>(), wp, reinterpret_cast<__nv_bfloat16*>(drows.data_ptr()),
         need_dw ? dw.data_ptr<float>() : nullptr, tokens, k, h);
@@ -185,7 +198,7 @@ void moe_zero_padding(at::Tensor& buf, const at::Tensor& src, const c10::optiona
   const int h = static_cast<int>(buf.size(1));
   if (rows == 0) return;
   c10::cuda::CUDAGuard guard(buf.device());
-  zero_rows_kernel<<<(rows + 7) / 8, 256, 0, stream()>>>(reinterpret_cast<__nv_bfloat16*>(buf.data_ptr()),
+  zero_rows_kernel<<<warp_grid(rows), 256, 0, stream()>>>(reinterpret_cast<__nv_bfloat16*>(buf.data_ptr()),
                                                           src.data_ptr<int32_t>(), rows, h, limit_ptr(row_limit));
   TDSV_LAUNCH_CHECK();
 }

@@ -304,3 +304,38 @@ def test_gemm_from_worker_thread():
     thread.join()
     assert not errors
     assert _rel(out, a.float() @ b.float().t()) < 1e-5
+
+
+@pytest.mark.parametrize("n,k,e", [(67, 2, 8), (5000, 8, 16), (3000, 8, 128), (1, 1, 4)])
+def test_moe_route_plan_matches_torch(n, k, e):
+    torch.manual_seed(11)
+    ids = torch.randint(-1, e, (n, k), dtype=torch.int32)
+    ref = M.build_routing(ids, e)  # CPU: torch stable sort
+    got = M.build_routing(ids.to(DEV), e)
+    assert got.capacity == ref.capacity
+    for name in ("route_rows", "src", "offsets", "rows", "counts", "total"):
+        assert torch.equal(getattr(got, name).cpu(), getattr(ref, name)), name
+
+
+def test_moe_route_plan_slabs():
+    torch.manual_seed(12)
+    slab, k, e = 64, 4, 8
+    ids = torch.randint(0, e, (3 * slab, k), dtype=torch.int32)
+    counts = torch.tensor([10, 0, 64], dtype=torch.int32)
+    ref = M.build_routing(ids, e, slab_counts=counts, slab=slab)
+    got = M.build_routing(ids.to(DEV), e, slab_counts=counts.to(DEV), slab=slab)
+    for name in ("route_rows", "src", "offsets", "rows", "counts", "total"):
+        assert torch.equal(getattr(got, name).cpu(), getattr(ref, name)), name
+    assert (got.route_rows.cpu()[10:slab] == -1).all()
+
+
+def test_ep_dest_plan():
+    torch.manual_seed(13)
+    t, k, ranks, per = 3000, 8, 8, 16
+    ids = torch.randint(0, ranks * per, (t, k), dtype=torch.int32, device=DEV)
+    dest, slot, counts = ops.ext().ep_dest_plan(ids, per, ranks)
+    want = torch.zeros(t, ranks, dtype=torch.bool, device=DEV)
+    want.scatter_(1, (ids // per).long(), True)
+    assert torch.equal(dest.bool(), want)
+    assert torch.equal(slot, (torch.cumsum(want.int(), 0) - 1).int())
+    assert torch.equal(counts, want.sum(0).int())

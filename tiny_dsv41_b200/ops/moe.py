@@ -31,9 +31,21 @@ class Routing:
     capacity: int
 
 
-def build_routing(ids: torch.Tensor, num_experts: int, block: int = BLOCK) -> Routing:
-    """Expert-major layout for ids [N, k] (entries < 0 are not routed)."""
+def build_routing(ids: torch.Tensor, num_experts: int, block: int = BLOCK, *, slab_counts=None,
+                  slab: int = 1) -> Routing:
+    """Expert-major layout for ids [N, k] (entries < 0 are not routed).
+
+    With ``slab_counts``, items are grouped in slabs of ``slab`` rows and only the first
+    ``slab_counts[s]`` items of slab ``s`` are routed (the rest count as unrouted).
+    """
     items, k = ids.shape
+    if ids.is_cuda:
+        route_rows, src, offsets, rows, counts, total = ext().moe_route_plan(
+            ids.to(torch.int32).contiguous(), num_experts, block, slab_counts, slab)
+        return Routing(route_rows, src, offsets, rows, counts, total, src.shape[0])
+    if slab_counts is not None:
+        live = (torch.arange(items, device=ids.device) % slab) < slab_counts.to(ids.device).repeat_interleave(slab)
+        ids = torch.where(live.unsqueeze(1), ids, torch.full_like(ids, -1))
     flat = ids.reshape(-1).long()
     n = flat.numel()
     valid = flat >= 0

@@ -119,20 +119,17 @@ class _Dispatch(torch.autograd.Function):
     def forward(ctx, x, weights, ids, ex: _Exchange):
         ws = ex.ws
         t, k = ids.shape
-        owners = torch.div(ids.long(), ex.e_local, rounding_mode="floor")
-        dest = torch.zeros(t, ws.ep, dtype=torch.bool, device=x.device)
-        dest.scatter_(1, owners, True)
-        ex.owner = owners
-        ex.dest_mask = dest.to(torch.uint8).contiguous()
-        ex.slot = (torch.cumsum(dest.to(torch.int32), dim=0) - 1).to(torch.int32).contiguous()
-        ex.counts = dest.sum(0).to(torch.int32).contiguous()
-        ex.push_to_receivers(x, ids.to(torch.int32).contiguous(), weights.float().contiguous())
+        ids32 = ids.to(torch.int32).contiguous()
+        ex.owner = torch.div(ids.long(), ex.e_local, rounding_mode="floor")
+        ex.dest_mask, ex.slot, ex.counts = ops.ext().ep_dest_plan(ids32, ex.e_local, ws.ep)
+        ex.push_to_receivers(x, ids32, weights.float().contiguous())
         ex.recv_counts = ws.flag_row(_COUNTS).clone()
         meta = ws.meta.view(ws.ep * ws.t_cap, 2 * k)
         live = (torch.arange(ws.t_cap, device=x.device).unsqueeze(0) < ex.recv_counts.unsqueeze(1)).reshape(-1, 1)
-        local_ids = torch.where(live, meta[:, :k], torch.full_like(meta[:, :k], -1))
         local_w = torch.where(live, meta[:, k:].view(torch.float32), torch.zeros_like(meta[:, k:].view(torch.float32)))
-        ex.routing = moe_ops.build_routing(local_ids, ex.e_local)
+        # rows past each source's live count are masked inside the routing plan
+        ex.routing = moe_ops.build_routing(meta[:, :k].contiguous(), ex.e_local, slab_counts=ex.recv_counts,
+                                           slab=ws.t_cap)
         rows = ops.ext().moe_gather(ws.recv.view(ws.ep * ws.t_cap, ws.hidden), ex.routing.src, ex.routing.total)
         ex.release_recv()
         ex.local_w = local_w.contiguous()

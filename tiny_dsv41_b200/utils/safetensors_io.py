@@ -11,6 +11,7 @@ from __future__ import annotations
 import json
 import mmap
 import struct
+import warnings
 from pathlib import Path
 
 import torch
@@ -55,7 +56,9 @@ class SafeTensorFile:
         raw = memoryview(self._map)[self.base + begin:self.base + end]
         if end == begin:
             return torch.empty(shape, dtype=dtype)
-        return torch.frombuffer(raw, dtype=torch.uint8).view(dtype).reshape(shape)
+        with warnings.catch_warnings():  # read-only map: callers copy (`tensor`) before any write
+            warnings.simplefilter("ignore", UserWarning)
+            return torch.frombuffer(raw, dtype=torch.uint8).view(dtype).reshape(shape)
 
     def tensor(self, name: str, device="cpu") -> torch.Tensor:
         return self._view(name).to(device, copy=True)
