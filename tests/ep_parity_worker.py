@@ -59,7 +59,13 @@ def main():
     e_local = e // world
     sl = slice(rank * e_local, (rank + 1) * e_local)
     failures = []
-    for name, cls in (("nvlink", NVLinkTokenDispatcher), ("nccl", AllToAllTokenDispatcher)):
+    from torch.utils.checkpoint import checkpoint
+
+    from tiny_dsv41_b200.parallel import replay
+
+    cases = [("nvlink", NVLinkTokenDispatcher, False), ("nccl", AllToAllTokenDispatcher, False),
+             ("nvlink-ckpt", NVLinkTokenDispatcher, True)]
+    for name, cls, ckpt in cases:
         for weighted_in_swiglu in (False, True):
             for trial in range(2):  # second trial exercises the epoch / free-flag reuse path
                 disp = cls(mesh)
@@ -68,8 +74,16 @@ def main():
                 wa = w.clone().requires_grad_()
                 w1 = w1_full[sl].clone().requires_grad_()
                 w2 = w2_full[sl].clone().requires_grad_()
-                out = experts_forward(disp, xa, ids, wa, w1, w2, weighted_in_swiglu)
-                out.backward(dout)
+                if ckpt:  # the recompute replays the recorded exchanges instead of repeating them
+                    out = checkpoint(experts_forward, disp, xa, ids, wa, w1, w2, weighted_in_swiglu,
+                                     use_reentrant=False, context_fn=replay.checkpoint_contexts)
+                    out.backward(dout)
+                    ws = disp._ws
+                    if (ws.recv_epoch, ws.ret_epoch) != (2, 2):
+                        failures.append((name, "exchanges", ws.recv_epoch, ws.ret_epoch))
+                else:
+                    out = experts_forward(disp, xa, ids, wa, w1, w2, weighted_in_swiglu)
+                    out.backward(dout)
                 local = TokenDispatcher()
                 local.expert_range(e)
                 xr = x.clone().requires_grad_()

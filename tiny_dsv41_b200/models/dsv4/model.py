@@ -19,6 +19,7 @@ from __future__ import annotations
 import math
 from contextlib import nullcontext
 from dataclasses import dataclass, fields, replace
+from functools import partial
 from pathlib import Path
 
 import numpy as np
@@ -30,6 +31,7 @@ from torch.utils.checkpoint import checkpoint
 
 from ... import ops
 from ...ops.router import AuxGradient
+from ...parallel import replay
 from ...parallel.cp import ContextParallel, ModelContext
 from ...parallel.dispatch import TokenDispatcher
 from ...parallel.engram_offload import CPUEmbeddingLookup
@@ -370,7 +372,7 @@ class DeepSeekV41Model(nn.Module):
         empty = hidden.new_empty(0)
         shadow = ShadowIndexers().dump(empty)
         use_ckpt = self.gradient_checkpointing and self.training and torch.is_grad_enabled()
-        loader = checkpoint if use_ckpt else _direct
+        loader = partial(checkpoint, context_fn=replay.checkpoint_contexts) if use_ckpt else _direct
         router_logits = []
         for layer in self.layers:
             device = next(layer.parameters()).device

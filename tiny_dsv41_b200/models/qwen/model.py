@@ -23,6 +23,7 @@ from torch.utils.checkpoint import checkpoint
 
 from ... import ops
 from ...ops.router import AuxGradient
+from ...parallel import replay
 from ...parallel.cp import ContextParallel
 from ...parallel.dispatch import TokenDispatcher
 from ..common import Linear, LMHead, fusable
@@ -209,7 +210,8 @@ class Qwen3MoeModel(nn.Module):
         collected = []
         for layer in self.layers:
             if self.gradient_checkpointing and self.training and torch.is_grad_enabled():
-                hidden, logits = checkpoint(layer, hidden, position_ids, attention_mask, use_reentrant=False)
+                hidden, logits = checkpoint(layer, hidden, position_ids, attention_mask, use_reentrant=False,
+                                            context_fn=replay.checkpoint_contexts)
             else:
                 hidden, logits = layer(hidden, position_ids, attention_mask)
             if output_router_logits and logits is not None:

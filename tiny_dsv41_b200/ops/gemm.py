@@ -59,11 +59,18 @@ def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
 
 
 def grouped_linear_reference(x, weight, offsets, rows):
-    out = x.new_zeros(x.shape[0], weight.shape[1])
-    for g, (start, count) in enumerate(zip(offsets.tolist(), rows.tolist())):
-        if count:
-            out[start:start + count] = (x[start:start + count].float() @ weight[g].float().t()).to(x.dtype)
-    return out
+    """Plain PyTorch restatement. Every group contributes a (possibly empty) product, so the result
+    always depends on ``x`` and ``weight`` in autograd, even when no rows are routed: a rank whose
+    experts received nothing must still run the same backward collectives as its peers."""
+    pieces, at = [], 0
+    for g, (start, count) in sorted(enumerate(zip(offsets.tolist(), rows.tolist())), key=lambda item: item[1][0]):
+        if start > at:
+            pieces.append(x.new_zeros(start - at, weight.shape[1]))
+        pieces.append((x[start:start + count].float() @ weight[g].float().t()).to(x.dtype))
+        at = max(at, start + count)
+    if at < x.shape[0]:
+        pieces.append(x.new_zeros(x.shape[0] - at, weight.shape[1]))
+    return torch.cat(pieces) if pieces else x.new_zeros(x.shape[0], weight.shape[1])
 
 
 class _GroupedLinear(torch.autograd.Function):

@@ -24,6 +24,12 @@ class ParallelMeshes:
     dense: "DeviceMesh | None" = None
     sparse: "DeviceMesh | None" = None
     engram: "DeviceMesh | None" = None
+    world: "DeviceMesh | None" = None
+
+    @property
+    def dense_world(self) -> "DeviceMesh | None":
+        """1-D mesh over every rank (dense FSDP when context parallelism splits sequences)."""
+        return self.world
 
     @property
     def cp_size(self) -> int:
@@ -46,9 +52,8 @@ class ParallelMeshes:
             raise ValueError(f"ep ({ep}) must divide world size ({world})")
         dense = init_device_mesh(device_type, (world // cp, cp), mesh_dim_names=("fsdp", "cp"))
         sparse = init_device_mesh(device_type, (world // ep, ep), mesh_dim_names=("expert_fsdp", "ep"))
-        engram_mesh = None
-        if engram:
-            engram_mesh = init_device_mesh(device_type, (world,), mesh_dim_names=("engram",))
+        world_mesh = init_device_mesh(device_type, (world,), mesh_dim_names=("world",))
+        engram_mesh = world_mesh if engram else None
         return cls(
             fsdp=dense["fsdp"],
             cp=dense["cp"] if cp > 1 else None,
@@ -57,6 +62,7 @@ class ParallelMeshes:
             dense=dense,
             sparse=sparse,
             engram=engram_mesh,
+            world=world_mesh,
         )
 
 

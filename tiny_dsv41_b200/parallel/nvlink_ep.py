@@ -21,6 +21,7 @@ import torch.distributed as dist
 
 from .. import ops
 from ..ops import moe as moe_ops
+from . import replay
 from .dispatch import DispatchBatch, TokenDispatcher
 
 # rows of the flag buffer
@@ -79,6 +80,10 @@ class _Exchange:
         self.routing = None
         self.local_w = None
         self.owner = None
+        self.recording = False  # activation-checkpoint replay (see parallel.replay)
+        self.replaying = False
+        self.cached_rows = None
+        self.cached_out = None
 
     # -- transfer primitives --------------------------------------------------------------
     def push_to_receivers(self, rows: torch.Tensor, ids=None, weights=None) -> None:
@@ -196,6 +201,25 @@ class _ScatterRowWeights(torch.autograd.Function):
         return g[torch.where(idx >= 0, idx, torch.full_like(idx, grad.shape[0]))], None, None
 
 
+class _ReplayDispatch(_Dispatch):
+    """Recompute of a recorded dispatch: the recorded rows, no transfer; same backward."""
+
+    @staticmethod
+    def forward(ctx, x, weights, ids, ex: _Exchange):
+        ctx.ex = ex
+        return ex.cached_rows, ex.local_w.clone()
+
+
+class _ReplayCombine(_Combine):
+    """Recompute of a recorded combine: the recorded output, no transfer; same backward."""
+
+    @staticmethod
+    def forward(ctx, y, local_w, ex: _Exchange):
+        ctx.ex = ex
+        ctx.save_for_backward(y, local_w)
+        return ex.cached_out
+
+
 class NVLinkTokenDispatcher(TokenDispatcher):
     """EP dispatcher whose transfers are this repository's peer-memory kernels."""
 
@@ -229,9 +253,19 @@ class NVLinkTokenDispatcher(TokenDispatcher):
             raise RuntimeError("attach the dispatcher to an expert module before use")
         if not x.is_cuda:
             raise RuntimeError("the NVLink dispatcher needs CUDA tensors")
-        ws = self._workspace(x.shape[0], x.shape[1], ids.shape[1], x.device)
-        ex = _Exchange(ws, x.shape[0], self.num_experts // self.size)
-        rows, local_w = _Dispatch.apply(x, weights, ids, ex)
+        handle, mode = replay.current()
+        if mode == "replay":
+            ex = handle.next()
+            rows, local_w = _ReplayDispatch.apply(x, weights, ids, ex)
+        else:
+            ws = self._workspace(x.shape[0], x.shape[1], ids.shape[1], x.device)
+            ex = _Exchange(ws, x.shape[0], self.num_experts // self.size)
+            rows, local_w = _Dispatch.apply(x, weights, ids, ex)
+            if mode == "record":
+                ex.recording = True
+                ex.cached_rows = rows.detach()
+                handle.record(ex)
+        ex.replaying = mode == "replay"
         routing = ex.routing
         return DispatchBatch(rows, routing.offsets, routing.rows, None,
                              {"exchange": ex, "local_w": local_w, "routing": routing}, routing.total)
@@ -242,7 +276,13 @@ class NVLinkTokenDispatcher(TokenDispatcher):
 
     def combine(self, y, batch: DispatchBatch, *, weighted: bool = True):
         ex = batch.state["exchange"]
-        return _Combine.apply(y, batch.state["local_w"] if weighted else None, ex)
+        local_w = batch.state["local_w"] if weighted else None
+        if ex.replaying:
+            return _ReplayCombine.apply(y, local_w, ex)
+        out = _Combine.apply(y, local_w, ex)
+        if ex.recording:
+            ex.cached_out = out.detach()
+        return out
 
 
 __all__ = ["NVLinkTokenDispatcher"]

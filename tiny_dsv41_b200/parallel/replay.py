@@ -1,0 +1,68 @@
+"""Expert-parallel exchange replay for activation checkpointing.
+
+With activation checkpointing a layer's forward runs twice: once in the forward pass and once
+again (recompute) during backward. Re-running the MoE token exchange would move the same rows
+over NVLink a second time. Instead, the first pass records what its exchanges produced (the
+received expert-major rows and the combined output, plus the routing state), and the recompute
+replays them: the recomputed graph gets the same tensors without any transfer, and its backward
+still runs the real reverse exchanges.
+
+``checkpoint_contexts`` is passed as ``context_fn`` to ``torch.utils.checkpoint.checkpoint``
+(non-reentrant): each checkpointed call gets one ``ReplayHandle``; the forward runs under its
+record context, the recompute under its replay context. The handle lives as long as the
+checkpoint frame, so recorded tensors are released after that layer's backward.
+"""
+
+from __future__ import annotations
+
+import threading
+
+_local = threading.local()
+
+
+class ReplayHandle:
+    def __init__(self) -> None:
+        self.items: list = []
+        self.cursor = 0
+
+    def record(self, item) -> None:
+        self.items.append(item)
+
+    def next(self):
+        if self.cursor >= len(self.items):
+            raise RuntimeError("recompute issued more expert exchanges than the recorded forward")
+        item = self.items[self.cursor]
+        self.cursor += 1
+        return item
+
+
+class _Mode:
+    def __init__(self, handle: ReplayHandle, mode: str) -> None:
+        self.handle, self.mode = handle, mode
+
+    def __enter__(self):
+        if self.mode == "replay":
+            self.handle.cursor = 0
+        stack = getattr(_local, "stack", None)
+        if stack is None:
+            stack = _local.stack = []
+        stack.append((self.handle, self.mode))
+        return self
+
+    def __exit__(self, *exc):
+        _local.stack.pop()
+        return False
+
+
+def checkpoint_contexts():
+    handle = ReplayHandle()
+    return _Mode(handle, "record"), _Mode(handle, "replay")
+
+
+def current():
+    """(handle, "record" | "replay") of the innermost checkpointed call, or (None, None)."""
+    stack = getattr(_local, "stack", None)
+    return stack[-1] if stack else (None, None)
+
+
+__all__ = ["ReplayHandle", "checkpoint_contexts", "current"]

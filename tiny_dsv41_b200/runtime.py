@@ -60,6 +60,7 @@ def initialize_runtime(
             os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
             os.environ.setdefault("MASTER_PORT", "29512")
             os.environ.setdefault("RANK", "0")
+            os.environ.setdefault("WORLD_SIZE", "1")
             kwargs = {"backend": "gloo"}
             if timeout:
                 kwargs["timeout"] = timeout
@@ -75,6 +76,7 @@ def initialize_runtime(
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         os.environ.setdefault("MASTER_PORT", "29512")
         os.environ.setdefault("RANK", "0")
+        os.environ.setdefault("WORLD_SIZE", "1")
         kwargs = {"backend": "nccl", "device_id": torch.device("cuda", local_rank)}
         if timeout:
             kwargs["timeout"] = timeout
