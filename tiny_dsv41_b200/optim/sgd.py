@@ -53,7 +53,16 @@ def install_sgd_in_backward(params, lr: float, *, expert_divisor: float = 1.0, e
         data = local_tensor(p.data)
         scale = grad_scale / state.divisors[id(p)]
         master = state.masters.get(id(p))
-        if data.is_cuda:
+        if grad.is_sparse:  # row-sparse embedding gradients (Engram tables): update only the touched rows
+            g = grad.coalesce()
+            rows, values = g.indices()[0], g.values().float() * scale
+            bad = (~torch.isfinite(values)).any().to(state.flag.dtype).reshape(1)
+            state.flag.copy_(torch.maximum(state.flag, bad.to(state.flag.device)))
+            target = master if master is not None else data
+            target.index_add_(0, rows.to(target.device), (-lr * values).to(device=target.device, dtype=target.dtype))
+            if master is not None:
+                data[rows] = master[rows].to(data.dtype)
+        elif data.is_cuda:
             target = master if master is not None else data
             out = data if (master is not None and data.dtype == torch.bfloat16) else None
             ext().sgd_step(target, grad.contiguous(), out, lr, scale, state.flag)

@@ -73,4 +73,45 @@ def apply_fsdp(model: nn.Module, meshes, *, param_dtype=torch.bfloat16, reduce_d
             module.set_modules_to_backward_prefetch([module])
 
 
-__all__ = ["apply_fsdp", "expert_parameters"]
+
+
+def scale_expert_grads(model: nn.Module, ep_size: int) -> None:
+    """Expert gradients arrive summed over the EP group's per-rank losses while FSDP averages the
+    dense ones over the world; dividing them by the EP size puts both on the same scale (the
+    expert-FSDP reduce-scatter, when experts are replicated, already divides by world / ep)."""
+    if ep_size <= 1:
+        return
+    for p in expert_parameters(model):
+        if p.grad is not None:
+            p.grad.mul_(1.0 / ep_size)
+
+
+@torch.no_grad()
+def clip_grad_norm_(parameters, max_norm: float) -> torch.Tensor:
+    """Global L2 norm over sharded (DTensor) and rank-local gradients, then in-place clipping.
+
+    Every rank holds a distinct piece of the gradient (FSDP shards, or this EP rank's experts),
+    so the squared norms of the local pieces sum to the global one with one all-reduce."""
+    import torch.distributed as dist
+
+    grads = [p.grad for p in parameters if p.grad is not None]
+    if not grads:
+        return torch.zeros(())
+    local = [g.to_local() if hasattr(g, "to_local") else g for g in grads]
+    device = local[0].device
+    sq = torch.zeros((), device=device, dtype=torch.float32)
+    for g in local:
+        sq += g.float().square().sum()
+    if dist.is_initialized():
+        dist.all_reduce(sq)
+    norm = sq.sqrt()
+    if not bool(torch.isfinite(norm)):
+        raise FloatingPointError("non-finite gradient norm; optimizer step not applied")
+    coef = min(1.0, max_norm / (float(norm) + 1e-6))
+    if coef < 1.0:
+        for g in local:
+            g.mul_(coef)
+    return norm
+
+
+__all__ = ["apply_fsdp", "clip_grad_norm_", "expert_parameters", "scale_expert_grads"]

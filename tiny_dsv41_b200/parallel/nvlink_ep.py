@@ -82,7 +82,7 @@ class _Exchange:
         self.owner = None
         self.recording = False  # activation-checkpoint replay (see parallel.replay)
         self.replaying = False
-        self.cached_rows = None
+        self.cached_recv = None
         self.cached_out = None
 
     # -- transfer primitives --------------------------------------------------------------
@@ -135,7 +135,10 @@ class _Dispatch(torch.autograd.Function):
         # rows past each source's live count are masked inside the routing plan
         ex.routing = moe_ops.build_routing(meta[:, :k].contiguous(), ex.e_local, slab_counts=ex.recv_counts,
                                            slab=ws.t_cap)
-        rows = ops.ext().moe_gather(ws.recv.view(ws.ep * ws.t_cap, ws.hidden), ex.routing.src, ex.routing.total)
+        received = ws.recv.view(ws.ep * ws.t_cap, ws.hidden)
+        rows = ops.ext().moe_gather(received, ex.routing.src, ex.routing.total)
+        if ex.recording:  # the receive slabs, not the capacity-sized expert-major buffer (~8x smaller)
+            ex.cached_recv = received.clone()
         ex.release_recv()
         ex.local_w = local_w.contiguous()
         ctx.ex = ex
@@ -207,7 +210,8 @@ class _ReplayDispatch(_Dispatch):
     @staticmethod
     def forward(ctx, x, weights, ids, ex: _Exchange):
         ctx.ex = ex
-        return ex.cached_rows, ex.local_w.clone()
+        rows = ops.ext().moe_gather(ex.cached_recv, ex.routing.src, ex.routing.total)
+        return rows, ex.local_w.clone()
 
 
 class _ReplayCombine(_Combine):
@@ -260,10 +264,9 @@ class NVLinkTokenDispatcher(TokenDispatcher):
         else:
             ws = self._workspace(x.shape[0], x.shape[1], ids.shape[1], x.device)
             ex = _Exchange(ws, x.shape[0], self.num_experts // self.size)
+            ex.recording = mode == "record"
             rows, local_w = _Dispatch.apply(x, weights, ids, ex)
-            if mode == "record":
-                ex.recording = True
-                ex.cached_rows = rows.detach()
+            if ex.recording:
                 handle.record(ex)
         ex.replaying = mode == "replay"
         routing = ex.routing

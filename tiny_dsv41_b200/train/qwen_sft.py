@@ -44,12 +44,14 @@ def _init_on_device(model: Qwen3MoeForCausalLM, seed: int, rank: int) -> None:
 
 class QwenTrainer:
     def __init__(self, config: Qwen3MoeConfig, *, lr: float = 1e-5, moment_dtype=torch.float32,
-                 dispatcher: str = "auto", gradient_checkpointing: bool = True, seed: int = 0) -> None:
+                 dispatcher: str = "auto", gradient_checkpointing: bool = True, seed: int = 0,
+                 tokens_per_rank: int = 4096) -> None:
         self.runtime = initialize_runtime(require_distributed=int(os.environ.get("WORLD_SIZE", "1")) > 1,
                                           timeout_seconds=900)
         rt = self.runtime
         torch.manual_seed(seed)
         self.world = rt.world_size
+        self.tokens_per_rank = tokens_per_rank  # sizes the NVLink receive slabs
         self.meshes = None
         cp = ContextParallel()
         if self.world > 1:
@@ -83,7 +85,7 @@ class QwenTrainer:
             try:
                 from ..parallel.nvlink_ep import NVLinkTokenDispatcher
 
-                return NVLinkTokenDispatcher(self.meshes.ep)
+                return NVLinkTokenDispatcher(self.meshes.ep, max_tokens=self.tokens_per_rank)
             except ImportError:
                 if kind == "nvlink":
                     raise
@@ -138,7 +140,8 @@ class QwenSFTBench:
         self.args = args
         config = Qwen3MoeConfig(num_hidden_layers=args.layers, max_window_layers=args.layers)
         moment = torch.float32 if args.moment_dtype == "fp32" else torch.bfloat16
-        self.trainer = QwenTrainer(config, lr=args.lr, moment_dtype=moment, dispatcher=args.dispatcher)
+        self.trainer = QwenTrainer(config, lr=args.lr, moment_dtype=moment, dispatcher=args.dispatcher,
+                                   tokens_per_rank=args.batch_size * args.seq_len)
         self.config = config
 
     def _batch(self, gen: torch.Generator):
@@ -210,10 +213,11 @@ class QwenSFTBench:
             e2e_losses.append(loss.item())
         torch.cuda.synchronize()
         wall_s = time.perf_counter() - wall0
-        times = torch.tensor([device_ms, wall_s * 1000.0], device=rt.device)
+        peak_gib = torch.cuda.max_memory_allocated(rt.device) / 2 ** 30
+        times = torch.tensor([device_ms, wall_s * 1000.0, peak_gib], device=rt.device)
         if dist.is_initialized():
             dist.all_reduce(times, op=dist.ReduceOp.MAX)
-        device_ms, wall_ms = times.tolist()
+        device_ms, wall_ms, peak_gib = times.tolist()
         tokens = a.batch_size * a.seq_len * rt.world_size * a.steps
         value = tokens / (device_ms / 1000.0)
         e2e = tokens / (wall_ms / 1000.0)
@@ -227,6 +231,7 @@ class QwenSFTBench:
             "other_launches_per_step": launches["other"],
             "loss": final_loss,
             "e2e_last_loss": e2e_losses[-1],
+            "peak_memory_gib": round(peak_gib, 2),
             "clocks": clocks.summary(),
             "config": {
                 "model": MODEL_NAME if self.config.num_hidden_layers == 48 else f"REDUCED {self.config.num_hidden_layers}L (not the benchmark)",

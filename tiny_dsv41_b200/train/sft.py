@@ -29,6 +29,7 @@ import torch
 import torch.distributed as dist
 
 from ..lora import LoRAConfig, adapter_parameters, inject_lora, save_adapter
+from ..parallel.fsdp import scale_expert_grads
 from ..rl.checkpoint import run_identity
 from ..rl.tokenizer import ModelTokenizer
 from ..runtime import initialize_runtime, local_tensor
@@ -201,17 +202,6 @@ def _loss(model, batch, family, runtime):
     return loss
 
 
-def _expert_scale(model, ep_size: int) -> None:
-    """Expert gradients arrive summed over the EP group's tokens; FSDP averages the dense ones."""
-    if ep_size <= 1:
-        return
-    from ..parallel.fsdp import expert_parameters
-
-    for p in expert_parameters(model):
-        if p.grad is not None:
-            p.grad.mul_(1.0 / ep_size)
-
-
 def train_update(model, optimizer, batches, *, family, runtime, cp_size=1, ep_size=1) -> dict:
     counts = [int((b["labels"][:, 1:] != -100).sum()) for b in batches]
     totals = torch.tensor([sum(counts), sum(int(b["attention_mask"].sum()) for b in batches)],
@@ -226,7 +216,7 @@ def train_update(model, optimizer, batches, *, family, runtime, cp_size=1, ep_si
         loss = _loss(model, batch, family, runtime)
         (loss * ((runtime.world_size // cp_size) * count / totals[0])).backward()
         weighted += loss.detach().double() * count
-    _expert_scale(model, ep_size)
+    scale_expert_grads(model, ep_size)
     finite = torch.ones((), device=runtime.device, dtype=torch.int32)
     for p in model.parameters():
         if p.requires_grad and p.grad is not None:
