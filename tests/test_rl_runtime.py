@@ -111,3 +111,15 @@ def test_local_grpo_run_and_resume(tmp_path):
     assert resumed == out / "step-00000003.pt"
     with pytest.raises(FileExistsError):
         run_training(model_dir=MODEL, data_path=data, config=RLConfig.from_dict(cfg), random_init=True)
+    # standalone sampling and evaluation from the saved checkpoint
+    from tiny_dsv41_b200.rl.evaluate import main as evaluate_main
+    from tiny_dsv41_b200.rl.sample import sample_checkpoint
+
+    result = sample_checkpoint(model_dir=MODEL, checkpoint=resumed, prompt_ids=[1, 2, 3], seed=5)
+    assert result["policy_version"] == 3 and len(result["response_ids"]) == 3
+    again = sample_checkpoint(model_dir=MODEL, checkpoint=resumed, prompt_ids=[1, 2, 3], seed=5)
+    assert again["response_ids"] == result["response_ids"]
+    evaluate_main(["--model-dir", str(MODEL), "--checkpoint", str(resumed), "--data", str(data), "--output-dir",
+                   str(tmp_path / "eval")])
+    metrics = json.loads((tmp_path / "eval" / "eval-metrics.jsonl").read_text().splitlines()[-1])
+    assert metrics["step"] == 3 and metrics["prompts"] == 4

@@ -128,7 +128,7 @@ def validate_policy_ack(ack: dict, artifact: dict) -> None:
 def save_training_checkpoint(path, model, optimizer, *, step: int, config, identity: dict, next_group_id: int,
                              rollout_rng_state, dropped_groups: int, manager_state=None,
                              policy_publication=None) -> None:
-    payload = {"format": FORMAT_VERSION, "step": step, "policy": policy_state(model),
+    payload = {"format_version": FORMAT_VERSION, "step": step, "policy": policy_state(model),
                "optimizer": optimizer.state_dict(), "config": config.to_dict(), "identity": identity,
                "next_group_id": next_group_id, "rollout_rng_state": rollout_rng_state,
                "learner_rng_state": torch.get_rng_state(), "dropped_groups": dropped_groups,
@@ -140,7 +140,7 @@ def save_training_checkpoint(path, model, optimizer, *, step: int, config, ident
 
 def load_training_checkpoint(path, model, optimizer, config, identity: dict) -> dict:
     state = torch.load(path, map_location="cpu", weights_only=False)
-    if state.get("format") not in (1, FORMAT_VERSION):
+    if state.get("format_version") not in (1, FORMAT_VERSION):
         raise ValueError("unsupported RL checkpoint format")
     validate_identity(state["identity"], identity)
     saved = dict(state["config"])
