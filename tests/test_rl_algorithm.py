@@ -64,3 +64,21 @@ def test_response_log_probs_dsv4_matches_reference():
     a = A.response_log_probs_batch(mine, prompts, responses, 0.8)
     b = R.response_log_probs_batch(ref, prompts, responses, 0.8)
     assert all(torch.allclose(x, y, atol=1e-5) for x, y in zip(a, b))
+
+
+def test_gsm8k_selection_and_metrics(tmp_path):
+    from pathlib import Path
+
+    from tiny_dsv41_b200.rl.gsm8k import formatting_correct, select_records, wilson_interval
+    from tiny_dsv41_b200.rl.tokenizer import ModelTokenizer
+
+    tok = ModelTokenizer(Path(__file__).resolve().parents[1] / "examples" / "tiny-dsv41")
+    rows = [{"id": f"gsm8k:train:{i}", "question": "what is the sum of 1 and " + "2 " * i, "answer": "3"}
+            for i in range(6)]
+    selected, excluded = select_records(rows, rows[:3], tok, max_prompt_tokens=27, max_train_groups=2,
+                                        eval_questions=1)
+    assert len(selected["train"]) == 2 and all(len(r.prompt_ids) <= 27 for r in selected["train"])
+    assert len(excluded["train"]) + 2 <= len(rows)
+    assert formatting_correct("so #### 42") and not formatting_correct("42")
+    low, high = wilson_interval(5, 10)
+    assert 0.23 < low < 0.24 and 0.76 < high < 0.77
