@@ -82,3 +82,26 @@ def test_gsm8k_selection_and_metrics(tmp_path):
     assert formatting_correct("so #### 42") and not formatting_correct("42")
     low, high = wilson_interval(5, 10)
     assert 0.23 < low < 0.24 and 0.76 < high < 0.77
+
+
+def test_learner_batch_planner_matches_reference():
+    import random
+
+    from tests.ref_oracle import import_reference, reference_available
+    from tiny_dsv41_b200.rl import learner_batch_planner as P
+
+    cells = P.parse_learner_batch_shapes("4:512,8:256,2:2047")
+    rng = random.Random(0)
+    lengths = [rng.randrange(1, 2048) for _ in range(32)]
+    plan = P.plan_learner_microbatches(lengths, 4, cells)
+    covered = sorted(i for b in plan for i in b["response_indices"])
+    assert covered == list(range(32))
+    own = [P.plan_response_ownership(lengths, r, 3) for r in range(3)]
+    assert len({len(o) for o in own}) == 1
+    if reference_available():
+        import_reference()
+        from dsv41_train.rl import learner_batch_planner as R
+
+        assert R.parse_learner_batch_shapes("4:512,8:256,2:2047") == cells
+        assert R.plan_learner_microbatches(lengths, 4, cells) == plan
+        assert [R.plan_response_ownership(lengths, r, 3) for r in range(3)] == own
