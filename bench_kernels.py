@@ -1,0 +1,141 @@
+"""Single-GPU microbenchmarks of the hot kernels, reported against the measured roofline.
+
+    python bench_kernels.py                      # every case, JSON lines
+    python bench_kernels.py --case grouped_fwd   # one case
+    python bench_kernels.py --case grouped_fwd --once   # warm up, then exactly one launch (for ncu)
+
+Each case times its kernel with CUDA events on the launching stream after warm-up (inputs are
+larger than the 126 MB L2 unless noted) and reports achieved TFLOP/s or GB/s and the fraction of
+``MEASURED_PEAKS.json`` (cuBLAS bf16 burst / copy bandwidth measured on this hardware); GEMM
+cases also time ``torch.matmul`` (cuBLAS) on the same operands.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+
+
+def _peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"tflops": p["bf16_tflops"], "gbs": p["hbm_gbs"], "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"tflops": 1590.0, "gbs": 6650.0, "source": "fallback"}
+
+
+def _time(fn, iters: int) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(iters):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / iters
+
+
+def cases():
+    from tiny_dsv41_b200 import ops
+
+    C = ops.ext()
+    dev = "cuda"
+    bf = torch.bfloat16
+
+    def dense(m, n, k):
+        a = torch.randn(m, k, device=dev, dtype=bf)
+        b = torch.randn(n, k, device=dev, dtype=bf)
+        out = torch.empty(m, n, device=dev, dtype=bf)
+        return (lambda: C.gemm(a, b, out, False, False, False)), (lambda: torch.matmul(a, b.t())), 2 * m * n * k, None
+
+    def grouped(kind, experts=16, per=2048, h=2048, inter=768):
+        rows = experts * per
+        off = torch.arange(experts, device=dev, dtype=torch.int32) * per
+        size = torch.full((experts,), per, device=dev, dtype=torch.int32)
+        x = torch.randn(rows, h, device=dev, dtype=bf)
+        w1 = torch.randn(experts, 2 * inter, h, device=dev, dtype=bf) * 0.02
+        gu = torch.randn(rows, 2 * inter, device=dev, dtype=bf)
+        flops = 2 * rows * 2 * inter * h
+        if kind == "fwd":
+            out = torch.empty(rows, 2 * inter, device=dev, dtype=bf)
+            return (lambda: C.grouped_gemm_m(x, w1, off, size, out, False, rows)), None, flops, None
+        if kind == "dx":
+            out = torch.empty(rows, h, device=dev, dtype=bf)
+            return (lambda: C.grouped_gemm_m(gu, w1, off, size, out, True, rows)), None, flops, None
+        out = torch.empty(experts, 2 * inter, h, device=dev, dtype=bf)
+        return (lambda: C.grouped_gemm_k(gu, x, off, size, out, False)), None, flops, None
+
+    def adamw(n=256 << 20):
+        p = torch.randn(n, device=dev)
+        g = torch.randn(n, device=dev, dtype=bf)
+        m = torch.zeros(n, device=dev)
+        v = torch.zeros(n, device=dev)
+        out = torch.empty(n, device=dev, dtype=bf)
+        step = (lambda: C.adamw_step(p, g, m, v, out, 1e-4, 0.9, 0.95, 1e-8, 0.1, 1, 1.0, None))
+        return step, None, None, n * (4 + 2 + 4 + 4 + 4 + 4 + 4 + 2)
+
+    def swiglu(rows=65536, inter=768):
+        gu = torch.randn(rows, 2 * inter, device=dev, dtype=bf)
+        return (lambda: C.swiglu_fwd(gu, None, False, 0.0, None)), None, None, rows * inter * 2 * 3
+
+    def rmsnorm(rows=32768, h=4096):
+        x = torch.randn(rows, h, device=dev, dtype=bf)
+        w = torch.ones(h, device=dev, dtype=bf)
+        return (lambda: C.rmsnorm_fwd(x, w, 1e-6)), None, None, rows * h * 2 * 2
+
+    return {
+        "dense_lm_head": lambda: dense(4096, 151936, 2048),
+        "dense_qkv": lambda: dense(4096, 5120, 2048),
+        "dense_8192": lambda: dense(8192, 8192, 8192),
+        "grouped_fwd": lambda: grouped("fwd"),
+        "grouped_dx": lambda: grouped("dx"),
+        "grouped_dw": lambda: grouped("dw"),
+        "adamw": adamw,
+        "swiglu": swiglu,
+        "rmsnorm": rmsnorm,
+    }
+
+
+def main(argv=None) -> None:
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--case", default="all")
+    p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--once", action="store_true", help="warm up, then launch the case exactly once")
+    args = p.parse_args(argv)
+    peaks = _peaks()
+    table = cases()
+    names = list(table) if args.case == "all" else [args.case]
+    for name in names:
+        fn, ref, flops, nbytes = table[name]()
+        if args.once:
+            for _ in range(2):
+                fn()
+            torch.cuda.synchronize()
+            fn()
+            torch.cuda.synchronize()
+            continue
+        ms = _time(fn, args.iters)
+        row = {"case": name, "ms": round(ms, 4)}
+        if flops:
+            row.update(tflops=round(flops / ms / 1e9, 1), frac_of_peak=round(flops / ms / 1e9 / peaks["tflops"], 3))
+        if nbytes:
+            row.update(gbs=round(nbytes / ms / 1e6, 1), frac_of_peak=round(nbytes / ms / 1e6 / peaks["gbs"], 3))
+        if ref is not None:
+            rms = _time(ref, args.iters)
+            row.update(cublas_ms=round(rms, 4), cublas_tflops=round(flops / rms / 1e9, 1))
+        row["peak_source"] = peaks["source"]
+        print(json.dumps(row), flush=True)
+        del fn, ref
+        torch.cuda.empty_cache()
+
+
+if __name__ == "__main__":
+    main()
