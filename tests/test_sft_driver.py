@@ -82,3 +82,44 @@ def test_ep2_fsdp2_matches_single_process(qwen_dir, tmp_path):
     a, _ = _losses(tmp_path / "one")
     b, _ = _losses(tmp_path / "two")
     assert b == pytest.approx(a, rel=1e-5)
+
+
+@pytest.fixture(scope="module")
+def dsv4_dir(tmp_path_factory):
+    from tiny_dsv41_b200.models.dsv4 import DeepSeekV41Config, DeepSeekV41ForCausalLM
+    from tiny_dsv41_b200.models.dsv4.checkpoint import write_released_checkpoint
+
+    root = tmp_path_factory.mktemp("dsv4sft")
+    torch.manual_seed(0)
+    write_released_checkpoint(DeepSeekV41ForCausalLM(DeepSeekV41Config.tiny()), root / "model")
+    for name in ("tokenizer.json", "tokenizer_config.json"):
+        shutil.copy(ROOT / "examples" / "tiny-dsv41" / name, root / "model" / name)
+    with (root / "data.jsonl").open("w") as f:
+        for a, b in [(1, 2), (2, 3), (3, 4), (4, 5)]:
+            f.write(json.dumps({"prompt": f"what is the sum of {a} and {b}", "answer": f"{a + b} <eos>"}) + "\n")
+    return root
+
+
+def _dsv4(rank, world, root, out, extra):
+    from tiny_dsv41_b200.runtime import initialize_runtime
+    from tiny_dsv41_b200.train.sft import parse_args, train
+
+    args = parse_args(["--model-path", str(root / "model"), "--data", str(root / "data.jsonl"), "--output-dir",
+                       str(out), "--family", "dsv4", "--batch-size", "1", "--seq-len", "64", "--learning-rate",
+                       "5e-2", "--device", "cpu", "--mode", "full", "--optimizer", "sgd", "--engram-offload",
+                       *extra])
+    train(args, initialize_runtime("cpu", require_distributed=True))
+
+
+def test_dsv4_full_sft_engram_rows_resume(dsv4_dir, tmp_path):
+    run_gloo(_dsv4, 1, dsv4_dir, tmp_path / "a", ["--steps", "3"])
+    run_gloo(_dsv4, 1, dsv4_dir, tmp_path / "b", ["--steps", "1"])
+    snap = torch.load(tmp_path / "b" / "checkpoint-00000001" / "rank-00000.pt", weights_only=False)
+    rows = snap["engram_rows"]["tables"]
+    assert rows and all(r["indices"].numel() > 0 for r in rows.values())
+    assert not any(".engram_tables." in n for n in snap["parameters"])
+    run_gloo(_dsv4, 1, dsv4_dir, tmp_path / "b", ["--steps", "3", "--resume", str(tmp_path / "b" / "checkpoint-00000001")])
+    a, sa = _losses(tmp_path / "a")
+    b, sb = _losses(tmp_path / "b")
+    assert b[-2:] == pytest.approx(a[-2:], rel=1e-5)
+    assert sb["eval_loss_after"] == pytest.approx(sa["eval_loss_after"], rel=1e-5)

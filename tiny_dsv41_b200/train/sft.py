@@ -273,6 +273,12 @@ def train(args, runtime) -> dict:
     params = [p for p in model.parameters() if p.requires_grad]
     opt_type = torch.optim.SGD if args.optimizer == "sgd" else torch.optim.AdamW
     optimizer = opt_type(params, lr=args.learning_rate, weight_decay=0, foreach=False)
+    if args.family == "dsv4" and args.optimizer == "sgd" and (args.mode == "full" or args.train_engram):
+        from ..parallel.engram_offload import install_engram_sgd_hooks
+        from .sft_engram import build_engram_checkpoint
+
+        install_engram_sgd_hooks(model, optimizer)
+        model._sft_engram_checkpoint = build_engram_checkpoint(model, args.model_path, optimizer)
     step, cursor = load_checkpoint(args.resume, model, optimizer, identity=identity) if args.resume else (0, 0)
     expected = step * args.gradient_accumulation_steps * args.batch_size * (runtime.world_size // args.cp_size)
     if cursor != expected:

@@ -42,7 +42,9 @@ def _layout(t) -> dict:
 
 
 def _tensors(model):
-    params = {n: p for n, p in model.named_parameters() if p.requires_grad}
+    manager = getattr(model, "_sft_engram_checkpoint", None)
+    rows = manager.parameter_names if manager is not None else frozenset()
+    params = {n: p for n, p in model.named_parameters() if p.requires_grad and n not in rows}
     buffers = {}
     for prefix, module in model.named_modules():
         for name, value in module.named_buffers(recurse=False):
@@ -61,15 +63,21 @@ def _ownership(model) -> dict:
 def _schema(model, optimizer) -> dict:
     params, buffers = _tensors(model)
     names = {id(p): n for n, p in params.items()}
+    manager = getattr(model, "_sft_engram_checkpoint", None)
+    if manager is not None:  # row-snapshot tables are optimizer members without saved state
+        names.update({id(t.weight): n for n, t in manager.tables.items()})
     groups = []
     for group in optimizer.param_groups:
         if any(id(p) not in names for p in group["params"]):
             raise ValueError("optimizer must contain only trainable model parameters")
         groups.append({"params": [names[id(p)] for p in group["params"]],
                        **{k: v for k, v in group.items() if k != "params" and isinstance(v, (int, float, bool, str))}})
-    return {"parameters": {n: _layout(p) for n, p in params.items()},
-            "buffers": {n: _layout(b) for n, b in buffers.items()}, "ownership": _ownership(model),
-            "optimizer": {"type": type(optimizer).__name__, "groups": groups}}
+    schema = {"parameters": {n: _layout(p) for n, p in params.items()},
+              "buffers": {n: _layout(b) for n, b in buffers.items()}, "ownership": _ownership(model),
+              "optimizer": {"type": type(optimizer).__name__, "groups": groups}}
+    if manager is not None:
+        schema["engram_rows"] = manager.schema
+    return schema
 
 
 def _digest(value) -> str:
@@ -90,6 +98,8 @@ def _optimizer_state(optimizer, params) -> dict:
     names = {id(p): n for n, p in params.items()}
     state = {}
     for p, fields in optimizer.state.items():
+        if id(p) not in names:  # Engram row tables: plain SGD keeps no state
+            continue
         state[names[id(p)]] = {k: (_local(v).detach().cpu().clone() if isinstance(v, torch.Tensor) else v)
                                for k, v in fields.items()}
     return state
@@ -111,6 +121,9 @@ def save_checkpoint(directory, model, optimizer, *, step: int, identity: dict, d
                "parameters": {n: _local(p).detach().cpu().clone() for n, p in params.items()},
                "buffers": {n: _local(b).detach().cpu().clone() for n, b in buffers.items()},
                "optimizer": _optimizer_state(optimizer, params)}
+    manager = getattr(model, "_sft_engram_checkpoint", None)
+    if manager is not None:
+        payload["engram_rows"] = manager.state_dict()
     path = directory / f"rank-{rank:05d}.pt"
     atomic_save(payload, path)
     records = _gather({"rank": rank, "sha256": file_sha256(path), "schema": _digest(schema)})
@@ -160,6 +173,9 @@ def load_checkpoint(directory, model, optimizer, *, identity: dict) -> tuple[int
     if _digest(schema) != record["schema"] or _digest(payload["schema"]) != record["schema"]:
         raise ValueError("SFT checkpoint topology differs from the current model and optimizer")
     params, buffers = _tensors(model)
+    manager = getattr(model, "_sft_engram_checkpoint", None)
+    if manager is not None:
+        manager.validate(payload.get("engram_rows"))
     for n, p in params.items():
         _local(p).copy_(payload["parameters"][n])
     for n, b in buffers.items():
@@ -170,6 +186,8 @@ def load_checkpoint(directory, model, optimizer, *, identity: dict) -> tuple[int
         state[p] = {k: _restore_like(p, v) for k, v in fields.items()}
     optimizer.state.clear()
     optimizer.state.update(state)
+    if manager is not None:
+        manager.load_state_dict(payload["engram_rows"])
     gathered = _gather(manifest["step"])
     if len(set(gathered)) != 1:
         raise ValueError("ranks restored different steps")
