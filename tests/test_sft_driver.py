@@ -123,3 +123,19 @@ def test_dsv4_full_sft_engram_rows_resume(dsv4_dir, tmp_path):
     b, sb = _losses(tmp_path / "b")
     assert b[-2:] == pytest.approx(a[-2:], rel=1e-5)
     assert sb["eval_loss_after"] == pytest.approx(sa["eval_loss_after"], rel=1e-5)
+
+
+def test_dsv4_lora_engram_bundle(dsv4_dir, tmp_path):
+    from tiny_dsv41_b200.rl.config import RLConfig
+    from tiny_dsv41_b200.train.sft_export import resolve_initial_bundle
+
+    out = tmp_path / "lora"
+    run_gloo(_dsv4, 1, dsv4_dir, out, ["--steps", "2", "--mode", "lora", "--train-engram"])
+    bundle = out / "sft-bundle-00000002"
+    manifest = json.loads((bundle / "manifest.json").read_text())
+    assert manifest["kind"] == "lora-engram-sft" and manifest["step"] == 2
+    delta = torch.load(bundle / "engram_delta.pt", weights_only=True)
+    assert all(t["indices"].numel() > 0 for t in delta["tables"].values())
+    cfg = RLConfig.from_dict(dict(trainable_scope="lora", initial_adapter=str(bundle), rollout_engine="native-pytorch"))
+    resolved = resolve_initial_bundle(cfg)
+    assert resolved.initial_adapter.endswith("adapter.pt") and resolved.initial_engram_delta.endswith("engram_delta.pt")

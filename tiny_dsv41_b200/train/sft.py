@@ -114,6 +114,12 @@ def validate_args(args, world_size: int) -> None:
         raise ValueError("trainable offloaded Engram requires SGD")
 
 
+def _backbone_layers(args) -> int:
+    from ..models.dsv4 import DeepSeekV41Config
+
+    return DeepSeekV41Config.from_json(Path(args.model_path) / "config.json").num_hidden_layers
+
+
 def lora_config(args) -> LoRAConfig:
     defaults = LoRAConfig().targets if args.family == "dsv4" else QWEN_LORA_TARGETS
     targets = tuple(n.strip() for n in args.lora_targets.split(",")) if args.lora_targets else defaults
@@ -337,10 +343,21 @@ def train(args, runtime) -> dict:
     after = evaluate(model, eval_batches, family=args.family, runtime=runtime, cp_size=args.cp_size)
     gen_after = generation_eval()
     if not args.no_save and args.mode == "lora" and step > 0 and (step > initial or args.resume):
-        base = {k: v for k, v in identity.items() if k not in {"training_config", "data_sha256", "eval_data_sha256"}}
-        save_adapter(model, out / "adapter.pt", base_identity=base)
-        if runtime.is_main:
-            (out / "adapter_metadata.json").write_text(json.dumps({"identity": identity, "step": step}, indent=2) + "\n")
+        if args.train_engram:
+            if args.engram_offload and args.lora_dropout == 0 and args.num_layers == _backbone_layers(args):
+                from .sft_export import export_sft_bundle
+
+                snapshot = Path(args.resume) if step == initial else out / f"checkpoint-{step:08d}"
+                bundle = export_sft_bundle(model, snapshot, args.model_path, out / f"sft-bundle-{step:08d}")
+                emit({"event": "sft_bundle_exported", "step": step, "path": str(bundle)})
+            else:
+                emit({"event": "sft_bundle_unavailable",
+                      "reason": "requires the complete backbone, dropout=0 and host-memory Engram"})
+        else:
+            base = {k: v for k, v in identity.items() if k not in {"training_config", "data_sha256", "eval_data_sha256"}}
+            save_adapter(model, out / "adapter.pt", base_identity=base)
+            if runtime.is_main:
+                (out / "adapter_metadata.json").write_text(json.dumps({"identity": identity, "step": step}, indent=2) + "\n")
     summary = {"event": "summary", "step": step, "initial_step": initial, "data_position": cursor,
                "checkpoint_saving": not args.no_save, "eval_loss_before": before, "eval_loss_after": after,
                "load_seconds": load_seconds, "loop_seconds": loop_seconds, "generation_before": gen_before,
