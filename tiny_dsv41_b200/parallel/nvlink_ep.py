@@ -209,8 +209,11 @@ class _ReplayDispatch(_Dispatch):
 
     @staticmethod
     def forward(ctx, x, weights, ids, ex: _Exchange):
+        if ex.cached_recv is None:
+            raise RuntimeError("the recorded dispatch was already replayed once")
         ctx.ex = ex
         rows = ops.ext().moe_gather(ex.cached_recv, ex.routing.src, ex.routing.total)
+        ex.cached_recv = None  # the backward needs only the routing state
         return rows, ex.local_w.clone()
 
 
@@ -219,9 +222,14 @@ class _ReplayCombine(_Combine):
 
     @staticmethod
     def forward(ctx, y, local_w, ex: _Exchange):
+        if ex.cached_out is None:
+            raise RuntimeError("the recorded combine was already replayed once")
         ctx.ex = ex
         ctx.save_for_backward(y, local_w)
-        return ex.cached_out
+        # A fresh output tensor: returning the recorded one would give it this node as grad_fn,
+        # and the record (held by the checkpoint frame) would then keep the frame alive.
+        out, ex.cached_out = ex.cached_out.clone(), None
+        return out
 
 
 class NVLinkTokenDispatcher(TokenDispatcher):
