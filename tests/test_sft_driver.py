@@ -139,3 +139,49 @@ def test_dsv4_lora_engram_bundle(dsv4_dir, tmp_path):
     cfg = RLConfig.from_dict(dict(trainable_scope="lora", initial_adapter=str(bundle), rollout_engine="native-pytorch"))
     resolved = resolve_initial_bundle(cfg)
     assert resolved.initial_adapter.endswith("adapter.pt") and resolved.initial_engram_delta.endswith("engram_delta.pt")
+
+
+def _dsv4_fsdp(rank, world, root, out, dump):
+    import torch.distributed as dist
+
+    from tiny_dsv41_b200.runtime import initialize_runtime
+    from tiny_dsv41_b200.train import sft
+
+    captured = {}
+    original = sft.load_model
+
+    def load_model(args, runtime):
+        model, meshes = original(args, runtime)
+        captured["model"] = model
+        return model, meshes
+
+    sft.load_model = load_model
+    args = sft.parse_args(["--model-path", str(root / "model"), "--data", str(root / "data.jsonl"), "--output-dir",
+                           str(out), "--family", "dsv4", "--batch-size", "1", "--seq-len", "64", "--learning-rate",
+                           "1e-2", "--device", "cpu", "--mode", "full", "--optimizer", "adamw", "--steps", "1",
+                           "--ep-size", "2"])
+    sft.train(args, initialize_runtime("cpu", require_distributed=True))
+    full = {}
+    for name, value in captured["model"].state_dict().items():
+        full[name] = value.full_tensor() if hasattr(value, "full_tensor") else value
+    if rank == 0:
+        torch.save({k: v for k, v in full.items() if ".routed." not in k and ".engram_tables." not in k}, dump)
+    # experts (EP) and Engram rows (row-sharded) are rank-local slices of the global tensor
+    torch.save({k: v for k, v in full.items() if ".routed." in k or ".engram_tables." in k}, f"{dump}.experts{rank}")
+    dist.barrier()
+
+
+def test_sft_source_rebuilds_fsdp_ep_snapshot(dsv4_dir, tmp_path):
+    from tiny_dsv41_b200.train.sft_source import SFTCheckpointSource
+
+    dump = tmp_path / "full.pt"
+    run_gloo(_dsv4_fsdp, 2, dsv4_dir, tmp_path / "run", str(dump))
+    source = SFTCheckpointSource(tmp_path / "run" / "checkpoint-00000001", dsv4_dir / "model")
+    rebuilt = source.state_dict()
+    dense = torch.load(dump)
+    for name, value in dense.items():
+        assert torch.equal(rebuilt[name].to(value.dtype), value), name
+    for rank in range(2):
+        for name, value in torch.load(f"{dump}.experts{rank}").items():
+            half = value.shape[0]
+            assert torch.equal(rebuilt[name][rank * half:(rank + 1) * half], value), name
