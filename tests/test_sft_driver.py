@@ -185,3 +185,22 @@ def test_sft_source_rebuilds_fsdp_ep_snapshot(dsv4_dir, tmp_path):
         for name, value in torch.load(f"{dump}.experts{rank}").items():
             half = value.shape[0]
             assert torch.equal(rebuilt[name][rank * half:(rank + 1) * half], value), name
+
+
+def test_rl_policy_from_sft_snapshot(dsv4_dir, tmp_path):
+    from tiny_dsv41_b200.rl.config import RLConfig
+    from tiny_dsv41_b200.rl.family import load_model_config
+    from tiny_dsv41_b200.rl.runtime import make_model
+
+    run_gloo(_dsv4, 1, dsv4_dir, tmp_path / "sft", ["--steps", "1"])
+    snapshot = tmp_path / "sft" / "checkpoint-00000001"
+    saved = torch.load(snapshot / "rank-00000.pt", weights_only=False)
+    cfg = RLConfig.from_dict(dict(rollout_engine="native-pytorch", initial_sft_checkpoint=str(snapshot)))
+    model_dir = dsv4_dir / "model"
+    policy = make_model(model_dir, load_model_config(model_dir), cfg, ("cpu",), False)
+    params = dict(policy.backend.named_parameters())
+    for name in ("model.layers.0.attention.q_a.weight", "model.layers.1.moe.routed.gate_up", "lm_head.weight"):
+        assert torch.equal(params[name].detach(), saved["parameters"][name].to(params[name].dtype)), name
+    rows = saved["engram_rows"]["tables"]["model.engram_tables.1.weight"]
+    table = policy.backend.model.engram_tables["1"].weight
+    assert torch.equal(table[rows["indices"]], rows["values"].to(table.dtype))

@@ -32,6 +32,17 @@ def lora_metadata(lora_config, initial_adapter) -> dict:
                                   "initial_adapter_sha256": file_sha256(initial_adapter) if initial_adapter else None}))
 
 
+def initial_sft_source(model_dir, model_config, config, random_init):
+    """The full-SFT snapshot named by ``initial_sft_checkpoint`` (DSV4 with pretrained base only)."""
+    if config.initial_sft_checkpoint is None:
+        return None
+    if random_init or getattr(model_config, "model_type", None) == "qwen3_moe":
+        raise ValueError("initial_sft_checkpoint requires a pretrained DSV4 base")
+    from ..train.sft_source import SFTCheckpointSource
+
+    return SFTCheckpointSource(config.initial_sft_checkpoint, model_dir)
+
+
 def load_model_config(model_dir):
     path = Path(model_dir) / "config.json"
     values = json.loads(path.read_text(encoding="utf-8"))
@@ -71,7 +82,10 @@ def load_model_config(model_dir):
 
 
 def build_policy(model_dir, model_config, *, random_init, devices, dtype, trainable_scope="all", lora_config=None,
-                 initial_adapter=None, engram_offload=True):
+                 initial_adapter=None, engram_offload=True, sft_source=None):
+    if sft_source is not None and (random_init or trainable_scope != "all"
+                                   or getattr(model_config, "model_type", None) == "qwen3_moe"):
+        raise ValueError("an SFT source requires a pretrained DSV4 base and trainable_scope=all")
     if (trainable_scope == "lora") != (lora_config is not None):
         raise ValueError("LoRA scope requires an explicit adapter configuration")
     if initial_adapter is not None and lora_config is None:
@@ -87,7 +101,7 @@ def build_policy(model_dir, model_config, *, random_init, devices, dtype, traina
             raise ValueError("DeepSeek RL requires trainable_scope=all or lora")
         model = build_dsv41_policy(model_dir, model_config, random_init=random_init, devices=devices, dtype=dtype,
                                    lora_config=lora_config, initial_adapter=initial_adapter,
-                                   engram_offload=engram_offload)
+                                   engram_offload=engram_offload, sft_source=sft_source)
     if lora_config is not None:
         model.lora_metadata = lora_metadata(lora_config, initial_adapter)
     return model

@@ -272,7 +272,7 @@ def _adapter(model_dir, lora_config, initial_adapter, random_init):
 
 
 def build_dsv41_policy(model_dir, config, *, random_init: bool, devices, dtype, lora_config: LoRAConfig | None = None,
-                       initial_adapter=None, engram_offload: bool = True):
+                       initial_adapter=None, engram_offload: bool = True, sft_source=None):
     from ..models.dsv4.model import DeepSeekV41ForCausalLM, NgramHash
 
     layer_device_map(config.num_hidden_layers, devices)
@@ -302,6 +302,15 @@ def build_dsv41_policy(model_dir, config, *, random_init: bool, devices, dtype, 
 
             token_map, _ = build_compressed_token_map(root / "tokenizer.json")
             backend.model.hash = NgramHash(config, backend.model.engram_layer_ids, token_map=token_map)
+    if sft_source is not None:  # a full-SFT snapshot replaces every base tensor it covers
+        targets = dict(backend.state_dict())
+        if sft_source.tensor_names - targets.keys():
+            raise ValueError("SFT snapshot holds tensors the policy does not have")
+        for name in sorted(sft_source.tensor_names):
+            sft_source.copy_tensor(name, targets[name])
+        for name, table in backend.model.engram_tables.items():
+            for ids, values in sft_source.iter_engram_rows(f"model.engram_tables.{name}.weight"):
+                table.weight.data.index_copy_(0, ids, values.to(table.weight.dtype))
     if lora_config is not None:
         inject_lora(backend, lora_config)
         adapter = _adapter(model_dir, lora_config, initial_adapter, random_init)

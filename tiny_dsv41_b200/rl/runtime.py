@@ -45,11 +45,16 @@ from .tokenizer import ModelTokenizer
 
 
 def make_model(model_dir, model_config, config: RLConfig, devices, random_init, *, role="learner"):
+    from ..train.sft_export import resolve_initial_bundle
+    from .family import initial_sft_source
+
+    config = resolve_initial_bundle(config)
     torch.manual_seed(config.seed)
     model = build_policy(model_dir, model_config, random_init=random_init, devices=devices,
                          dtype=getattr(torch, config.dtype), trainable_scope=config.trainable_scope,
                          lora_config=policy_lora_config(config, model_config), initial_adapter=config.initial_adapter,
-                         engram_offload=config.engram_offload)
+                         engram_offload=config.engram_offload,
+                         sft_source=initial_sft_source(model_dir, model_config, config, random_init))
     if getattr(model_config, "model_type", None) == "qwen3_moe":
         model.qwen_last_position_only = config.qwen_last_position_only
         model.qwen_kv_cache = config.qwen_kv_cache
@@ -172,6 +177,10 @@ def run_training(*, model_dir, data_path, config: RLConfig, random_init=False, r
     validate_reward_records(records + eval_records, reward_fn, config.reward)
     identity = run_identity(model_dir, data_path, random_init, eval_data_path=eval_data_path)
     identity["trainable_scope"] = config.trainable_scope
+    if config.initial_sft_checkpoint is not None:
+        from .family import initial_sft_source
+
+        identity["initial_sft_checkpoint"] = initial_sft_source(model_dir, model_config, config, random_init).identity
     if config.trainable_scope == "lora":
         identity["lora"] = {"rank": config.lora_rank, "alpha": config.lora_alpha,
                             "targets": list(policy_lora_config(config, model_config).targets)}
