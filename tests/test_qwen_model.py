@@ -60,3 +60,28 @@ def test_parity_with_reference_cpu():
         assert p.grad is not None and q.grad is not None, name
         err = (p.grad - q.grad).norm() / q.grad.norm().clamp_min(1e-12)
         assert err < 1e-4, (name, err.item())
+
+
+def test_kv_cache_sampling_matches_full_forward():
+    from tiny_dsv41_b200.models.qwen import Qwen3MoeConfig as Cfg
+    from tiny_dsv41_b200.rl.data import PromptRecord
+    from tiny_dsv41_b200.rl.policy import QwenPolicy
+    from tiny_dsv41_b200.rl.rollout import generate_group
+
+    torch.manual_seed(0)
+    cfg = Cfg.tiny(num_hidden_layers=2, max_window_layers=2, vocab_size=64)
+    from tiny_dsv41_b200.models.qwen import Qwen3MoeForCausalLM as M
+
+    policy = QwenPolicy(M(cfg), trainable_scope="lm_head")
+    record = PromptRecord([1, 5, 7, 9], target_ids=[3, 3])
+    runs = []
+    for cached in (False, True):
+        policy.qwen_kv_cache = cached
+        policy._session = None
+        gen = torch.Generator().manual_seed(3)
+        runs.append(generate_group(policy, record, 2, 6, 1.0, eos_token_id=None, policy_version=0, group_id=0,
+                                   generator=gen))
+    for a, b in zip(runs[0].samples, runs[1].samples):
+        assert a.response_ids == b.response_ids
+        assert a.behavior_log_probs == pytest.approx(b.behavior_log_probs, abs=1e-5)
+    assert policy._session.prefills == 2  # one per sample, every later token is incremental

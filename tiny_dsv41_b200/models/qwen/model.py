@@ -61,7 +61,7 @@ class Qwen3MoeAttention(nn.Module):
         self.q_norm = Qwen3MoeRMSNorm(self.head_dim, config.rms_norm_eps)
         self.k_norm = Qwen3MoeRMSNorm(self.head_dim, config.rms_norm_eps)
 
-    def forward(self, hidden, position_ids, attention_mask=None):
+    def forward(self, hidden, position_ids, attention_mask=None, cache=None):
         batch, length, _ = hidden.shape
         freqs = ops.rope.cached_freqs(("rope", self.head_dim, self.rope_theta),
                                       ops.inv_freq(self.head_dim, self.rope_theta), hidden.device)
@@ -77,6 +77,13 @@ class Qwen3MoeAttention(nn.Module):
         v = v.reshape(batch, length, self.num_key_value_heads, self.head_dim)
         cp = self.context_parallel
         mask = None
+        if cache is not None:  # incremental decoding: attend over cached keys/values of earlier positions
+            if cp.enabled:
+                raise ValueError("the KV cache does not support context parallelism")
+            k, v, key_positions = cache.append(self.layer_id, k, v, position_ids)
+            mask = key_positions[:, None, None, :] <= position_ids[:, None, :, None]
+            out = ops.causal_attention(q, k, v, mask=mask)
+            return self.o_proj(out.reshape(batch, length, -1))
         if cp.enabled:
             k = cp.gather(k, dim=1)
             v = cp.gather(v, dim=1)
@@ -166,8 +173,8 @@ class Qwen3MoeDecoderLayer(nn.Module):
         self.input_layernorm = Qwen3MoeRMSNorm(config.hidden_size, config.rms_norm_eps)
         self.post_attention_layernorm = Qwen3MoeRMSNorm(config.hidden_size, config.rms_norm_eps)
 
-    def forward(self, hidden, position_ids, attention_mask=None):
-        hidden = hidden + self.self_attn(self.input_layernorm(hidden), position_ids, attention_mask)
+    def forward(self, hidden, position_ids, attention_mask=None, cache=None):
+        hidden = hidden + self.self_attn(self.input_layernorm(hidden), position_ids, attention_mask, cache)
         out = self.mlp(self.post_attention_layernorm(hidden))
         logits = None
         if isinstance(out, tuple):
@@ -193,7 +200,7 @@ class Qwen3MoeModel(nn.Module):
         self.norm = Qwen3MoeRMSNorm(config.hidden_size, config.rms_norm_eps)
         self.gradient_checkpointing = False
 
-    def forward(self, input_ids, attention_mask=None, position_ids=None, *, output_router_logits=False):
+    def forward(self, input_ids, attention_mask=None, position_ids=None, *, output_router_logits=False, cache=None):
         if input_ids.ndim != 2:
             raise ValueError("input_ids must have shape [batch, sequence]")
         if input_ids.shape[1] > self.config.max_position_embeddings:
@@ -209,7 +216,9 @@ class Qwen3MoeModel(nn.Module):
         hidden = self.embed_tokens(input_ids)
         collected = []
         for layer in self.layers:
-            if self.gradient_checkpointing and self.training and torch.is_grad_enabled():
+            if cache is not None:
+                hidden, logits = layer(hidden, position_ids, attention_mask, cache)
+            elif self.gradient_checkpointing and self.training and torch.is_grad_enabled():
                 hidden, logits = checkpoint(layer, hidden, position_ids, attention_mask, use_reentrant=False,
                                             context_fn=replay.checkpoint_contexts)
             else:

@@ -236,8 +236,18 @@ class QwenPolicy(_PolicyBase):
         return self.backend.lm_head(hidden)
 
     def next_token_logits(self, input_ids, attention_mask=None):
+        if self.qwen_kv_cache and not torch.is_grad_enabled():
+            if getattr(self, "_session", None) is None:
+                from ..models.qwen.generation import IncrementalLogits
+
+                self._session = IncrementalLogits(self.backend)
+            return self._session(input_ids)
         logits = self(input_ids, attention_mask, last_position_only=self.qwen_last_position_only)
         return logits[:, -1]
+
+    def _load(self, state, destinations, what):
+        self._session = None  # cached keys/values belong to the previous weights
+        super()._load(state, destinations, what)
 
     def response_log_probs(self, prompt_ids, response_ids, temperature):
         """One forward per action over its exact sampling prefix (stop tokens included)."""
