@@ -43,7 +43,8 @@ def parse_args(argv=None):
     p.add_argument("--batch-size", type=int, default=1)
     p.add_argument("--layers", type=int, default=48, help="development only: fewer layers is not the benchmark")
     p.add_argument("--dispatcher", choices=("auto", "nccl", "nvlink"), default="auto")
-    p.add_argument("--moment-dtype", choices=("fp32", "bf16"), default="fp32")
+    p.add_argument("--moment-dtype", choices=("auto", "fp32", "bf16"), default="auto",
+                   help="auto: fp32 AdamW moments when they fit in HBM at this N, else bf16")
     p.add_argument("--lr", type=float, default=1e-5)
     return p.parse_args(argv)
 
@@ -95,8 +96,14 @@ def emit(record: dict) -> None:
     print(json.dumps(record), flush=True)
 
 
+HBM_BYTES = 178 * 2 ** 30       # usable B200 capacity reported by torch
+ACTIVATION_RESERVE = 24 * 2 ** 30  # recompute transients, logits, NVLink slabs, replay records, allocator slack
+
+
 def memory_plan(args, world: int) -> tuple[bool, str]:
-    """Whether the full optimizer state fits in HBM at this N (fp32 master + moments per rank)."""
+    """Whether the persistent training state fits in HBM at this N, choosing the moment dtype when
+    ``--moment-dtype auto``: bf16 params + fp32 master + fp32 (or bf16) AdamW moments per parameter.
+    Gradients are transient (the optimizer runs inside the backward pass)."""
     from tiny_dsv41_b200.models.qwen import Qwen3MoeConfig
 
     cfg = Qwen3MoeConfig(num_hidden_layers=args.layers, max_window_layers=args.layers)
@@ -105,13 +112,16 @@ def memory_plan(args, world: int) -> tuple[bool, str]:
                                       * cfg.head_dim * 2 + cfg.hidden_size * cfg.num_experts)
              + 2 * cfg.vocab_size * cfg.hidden_size)
     per_rank = experts / world + dense / world
-    moment_bytes = 8 if args.moment_dtype == "fp32" else 4
-    bytes_per_param = 2 + 2 + 4 + moment_bytes  # bf16 param + bf16 grad + fp32 master + moments
-    need = per_rank * bytes_per_param
-    budget = 160e9
-    return need <= budget, (f"{(experts + dense) / 1e9:.1f}B params; {per_rank / 1e9:.2f}B per rank x "
-                            f"{bytes_per_param} B (bf16 param+grad, fp32 master, {args.moment_dtype} moments) "
-                            f"= {need / 1e9:.0f} GB > {budget / 1e9:.0f} GB of HBM per B200")
+    budget = HBM_BYTES - ACTIVATION_RESERVE
+    choices = ("fp32", "bf16") if args.moment_dtype == "auto" else (args.moment_dtype,)
+    for moments in choices:
+        need = per_rank * (2 + 4 + (8 if moments == "fp32" else 4))
+        if need <= budget:
+            args.moment_dtype = moments
+            return True, f"{need / 2 ** 30:.0f} GiB of persistent state per rank ({moments} moments)"
+    return False, (f"{(experts + dense) / 1e9:.1f}B params; {per_rank / 1e9:.2f}B per rank x "
+                   f"{2 + 4 + (8 if choices[-1] == 'fp32' else 4)} B (bf16 param, fp32 master, {choices[-1]} moments) "
+                   f"= {need / 2 ** 30:.0f} GiB > {budget / 2 ** 30:.0f} GiB of HBM left after activations per B200")
 
 
 def run_native(args) -> None:
