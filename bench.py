@@ -125,6 +125,8 @@ def memory_plan(args, world: int) -> tuple[bool, str]:
 
 
 def run_native(args) -> None:
+    # grow allocator segments in place instead of new cudaMalloc calls (which synchronise the device)
+    os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
     import torch
     import torch.distributed as dist
 
