@@ -65,3 +65,21 @@ def test_qwen_training_step_reduces_loss():
         out.loss.backward()
         losses.append(out.loss.item())
     assert losses[-1] < losses[0] - 0.5, losses
+
+
+def test_kv_cache_decoding_gpu():
+    from tiny_dsv41_b200.models.qwen.generation import IncrementalLogits
+
+    torch.manual_seed(4)
+    cfg = Qwen3MoeConfig.tiny(num_hidden_layers=2, vocab_size=512)
+    model = Qwen3MoeForCausalLM(cfg).cuda().to(torch.bfloat16).eval()
+    inc = IncrementalLogits(model)
+    ids = [1, 17, 33, 250, 9, 77, 3]
+    with torch.no_grad():
+        for _ in range(5):
+            seq = torch.tensor([ids], device="cuda")
+            a = inc(seq).float()
+            b = model(seq).logits[:, -1].float()
+            assert _rel(a, b) < 2e-2
+            ids.append(int(b.argmax()))
+    assert inc.prefills == 1
