@@ -37,6 +37,7 @@ int64_t read_status();
 std::vector<at::Tensor> moe_route_plan(const at::Tensor& ids, int64_t num_experts, int64_t block,
                                        const c10::optional<at::Tensor>& slab_counts, int64_t slab);
 std::vector<at::Tensor> ep_dest_plan(const at::Tensor& ids, int64_t experts_per_rank, int64_t ranks);
+at::Tensor fp4_dequant(const at::Tensor& packed, const at::Tensor& scale);
 std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, double eps);
 std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
                                     const at::Tensor& rstd, bool need_dw);
@@ -122,6 +123,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ids"), py::arg("num_experts"), py::arg("block") = 128, py::arg("slab_counts") = py::none(),
         py::arg("slab") = 1);
   m.def("ep_dest_plan", &tdsv::ep_dest_plan, "per-token destination ranks, receive slots and counts");
+  m.def("fp4_dequant", &tdsv::fp4_dequant, "MXFP4 (E2M1 + E8M0 per 32) to bf16");
   m.def("rmsnorm_fwd", &tdsv::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &tdsv::rmsnorm_bwd);
   m.def("column_sum", &tdsv::column_sum);

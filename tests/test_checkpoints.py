@@ -2,6 +2,7 @@
 reference loader for parity."""
 
 import os
+import shutil
 
 import pytest
 import torch
@@ -67,3 +68,31 @@ def test_loader_parity_with_reference(tmp_path):
     ref_state = ref.state_dict()
     for name, value in mine.state_dict().items():
         assert torch.equal(value, ref_state[name]), name
+
+
+def test_frozen_fp4_experts_match_dequantised(tmp_path):
+    """Experts kept as MXFP4 codes give the same forward and input gradient as experts dequantised
+    at load (the same FP4 values either way)."""
+    from tiny_dsv41_b200.models.dsv4.checkpoint import load_dsv41_backbone_prefix
+    from tiny_dsv41_b200.ops.fp4 import dequantize_fp4
+
+    torch.manual_seed(0)
+    write_released_checkpoint(DeepSeekV41ForCausalLM(DeepSeekV41Config.tiny()), tmp_path)
+    shutil.copy(os.path.join(ROOT, "examples", "tiny-dsv41", "tokenizer.json"), tmp_path / "tokenizer.json")
+    dense = load_dsv41_backbone_prefix(tmp_path, num_layers=3, dtype=torch.float32)
+    packed = load_dsv41_backbone_prefix(tmp_path, num_layers=3, dtype=torch.float32, fp4_experts=True)
+    routed = packed.model.layers[1].moe.routed
+    assert routed.frozen_fp4 and not any("routed" in n for n, _ in packed.named_parameters())
+    expanded = dequantize_fp4(routed.gate_up_fp4, routed.gate_up_scale).float()
+    assert torch.equal(expanded, dense.model.layers[1].moe.routed.gate_up.detach().to(torch.bfloat16).float())
+    ids = torch.randint(0, 32, (1, 24))
+    emb = [m.model.embedding.weight for m in (dense, packed)]
+    for e in emb:
+        e.requires_grad_(True)
+    a = dense(ids, labels=ids)
+    b = packed(ids, labels=ids)
+    assert torch.allclose(a.loss, b.loss, rtol=2e-2), (a.loss, b.loss)
+    a.loss.backward()
+    b.loss.backward()
+    rel = (emb[0].grad - emb[1].grad).norm() / emb[0].grad.norm()
+    assert rel < 5e-2, rel

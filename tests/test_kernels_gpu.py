@@ -339,3 +339,39 @@ def test_ep_dest_plan():
     assert torch.equal(dest.bool(), want)
     assert torch.equal(slot, (torch.cumsum(want.int(), 0) - 1).int())
     assert torch.equal(counts, want.sum(0).int())
+
+
+def test_fp4_dequant_matches_torch():
+    from tiny_dsv41_b200.ops.fp4 import dequantize_fp4
+    from tiny_dsv41_b200.utils.quant import quantize_fp4_rows
+
+    torch.manual_seed(14)
+    w = torch.randn(96, 256) * 0.05
+    packed, scale = quantize_fp4_rows(w)
+    codes, scales = packed.view(torch.uint8), scale.view(torch.uint8)
+    ref = dequantize_fp4(codes, scales)  # CPU restatement
+    got = dequantize_fp4(codes.to(DEV), scales.to(DEV))
+    assert torch.equal(got.cpu(), ref)
+
+
+def test_frozen_fp4_grouped_linear_grad():
+    from tiny_dsv41_b200.ops.fp4 import dequantize_fp4, fp4_grouped_linear
+    from tiny_dsv41_b200.utils.quant import quantize_fp4_rows
+
+    torch.manual_seed(15)
+    e, n, k, per = 4, 256, 512, 128
+    packed, scale = quantize_fp4_rows(torch.randn(e * n, k) * 0.05)
+    codes = packed.view(torch.uint8).view(e, n, k // 2).to(DEV)
+    scales = scale.view(torch.uint8).view(e, n, k // 32).to(DEV)
+    x = torch.randn(e * per, k, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    off = torch.arange(e, device=DEV, dtype=torch.int32) * per
+    rows = torch.full((e,), per, device=DEV, dtype=torch.int32)
+    y = fp4_grouped_linear(x, codes, scales, off, rows, n)
+    g = torch.randn_like(y)
+    y.backward(g)
+    w = dequantize_fp4(codes, scales).float()
+    xr = x.detach().float().requires_grad_()
+    yr = torch.cat([xr[i * per:(i + 1) * per] @ w[i].t() for i in range(e)])
+    yr.backward(g.float())
+    assert _rel(y, yr) < 1e-2
+    assert _rel(x.grad, xr.grad) < 1e-2

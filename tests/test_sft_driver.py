@@ -204,3 +204,11 @@ def test_rl_policy_from_sft_snapshot(dsv4_dir, tmp_path):
     rows = saved["engram_rows"]["tables"]["model.engram_tables.1.weight"]
     table = policy.backend.model.engram_tables["1"].weight
     assert torch.equal(table[rows["indices"]], rows["values"].to(table.dtype))
+
+
+def test_dsv4_lora_sft_fp4_experts(dsv4_dir, tmp_path):
+    out = tmp_path / "fp4"
+    run_gloo(_dsv4, 1, dsv4_dir, out, ["--steps", "2", "--mode", "lora", "--fp4-experts", "--no-save"])
+    losses, summary = _losses(out)
+    assert len(losses) == 2 and all(l > 0 for l in losses)
+    assert summary["eval_loss_after"] < summary["eval_loss_before"]

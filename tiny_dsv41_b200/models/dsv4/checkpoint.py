@@ -85,7 +85,9 @@ def load_dsv41_backbone_window(folder, *, start_layer: int = 0, num_layers: int 
                                dtype=torch.bfloat16, context_parallel=None, token_dispatcher=None, engram_mesh=None,
                                sparse_engram_gradients: bool = False,
                                layer_loaded: Callable | None = None, engram_weights=None,
-                               engram_offload: bool = False) -> DeepSeekV41ForCausalLM:
+                               engram_offload: bool = False, fp4_experts: bool = False) -> DeepSeekV41ForCausalLM:
+    """``fp4_experts`` keeps the routed experts as frozen MXFP4 codes + E8M0 scales (uint8 buffers,
+    expanded per GEMM) instead of dequantising them to ``dtype`` at load."""
     folder = Path(folder)
     if engram_offload and engram_weights is not None:
         raise ValueError("trainable CPU offload cannot reuse frozen shared Engram weights")
@@ -130,16 +132,35 @@ def load_dsv41_backbone_window(folder, *, start_layer: int = 0, num_layers: int 
                 state[name] = value
             state["attention.o_a.weight"] = state["attention.o_a.weight"].view(config.o_groups, config.o_lora_rank, -1)
             routed = layer.moe.routed
-            gate_up = torch.empty(routed.gate_up.shape, device=target, dtype=dtype)
-            down = torch.empty(routed.down.shape, device=target, dtype=dtype)
-            for local, gid in enumerate(range(routed.expert_start, routed.expert_start + routed.num_experts)):
-                prefix = f"{src}.ffn.experts.{gid}"
-                w = lambda n: dequantize_fp4_rows(read(f"{prefix}.{n}.weight"), read(f"{prefix}.{n}.scale"), dtype=dtype)  # noqa: E731
-                gate_up[local, :, 0].copy_(w("w1"))
-                gate_up[local, :, 1].copy_(w("w3"))
-                down[local].copy_(w("w2"))
-            state["moe.routed.gate_up"] = gate_up
-            state["moe.routed.down"] = down
+            experts = range(routed.expert_start, routed.expert_start + routed.num_experts)
+            if fp4_experts:
+                e, i, h = routed.num_experts, routed.intermediate, routed.hidden_size
+                raw = lambda name: read(name).view(torch.uint8)  # noqa: E731
+                codes = {"gate_up_fp4": torch.empty(e, i, 2, h // 2, dtype=torch.uint8, device=target),
+                         "gate_up_scale": torch.empty(e, i, 2, h // 32, dtype=torch.uint8, device=target),
+                         "down_fp4": torch.empty(e, h, i // 2, dtype=torch.uint8, device=target),
+                         "down_scale": torch.empty(e, h, i // 32, dtype=torch.uint8, device=target)}
+                for local, gid in enumerate(experts):
+                    prefix = f"{src}.ffn.experts.{gid}"
+                    codes["gate_up_fp4"][local, :, 0].copy_(raw(f"{prefix}.w1.weight"))
+                    codes["gate_up_fp4"][local, :, 1].copy_(raw(f"{prefix}.w3.weight"))
+                    codes["gate_up_scale"][local, :, 0].copy_(raw(f"{prefix}.w1.scale"))
+                    codes["gate_up_scale"][local, :, 1].copy_(raw(f"{prefix}.w3.scale"))
+                    codes["down_fp4"][local].copy_(raw(f"{prefix}.w2.weight"))
+                    codes["down_scale"][local].copy_(raw(f"{prefix}.w2.scale"))
+                routed.freeze_fp4(*codes.values())
+                state.update({f"moe.routed.{k}": v for k, v in codes.items()})
+            else:
+                gate_up = torch.empty(routed.gate_up.shape, device=target, dtype=dtype)
+                down = torch.empty(routed.down.shape, device=target, dtype=dtype)
+                for local, gid in enumerate(experts):
+                    prefix = f"{src}.ffn.experts.{gid}"
+                    w = lambda n: dequantize_fp4_rows(read(f"{prefix}.{n}.weight"), read(f"{prefix}.{n}.scale"), dtype=dtype)  # noqa: E731
+                    gate_up[local, :, 0].copy_(w("w1"))
+                    gate_up[local, :, 1].copy_(w("w3"))
+                    down[local].copy_(w("w2"))
+                state["moe.routed.gate_up"] = gate_up
+                state["moe.routed.down"] = down
             comp = layer.attention.compressor
             if comp is not None:
                 state["attention.compressor.kv_proj.weight"] = read(f"{src}.attn.compressor.wkv.weight").to(dtype)

@@ -54,15 +54,44 @@ class RoutedExperts(nn.Module):
 
     @property
     def local_parameter_count(self) -> int:
+        if self.frozen_fp4:
+            return 2 * (self.gate_up_fp4.numel() + self.down_fp4.numel())
         return self.gate_up.numel() + self.down.numel()
+
+    @property
+    def frozen_fp4(self) -> bool:
+        return "gate_up_fp4" in self._buffers
+
+    def freeze_fp4(self, gate_up_fp4, gate_up_scale, down_fp4, down_scale) -> None:
+        """Replace the bf16 expert weights by frozen MXFP4 codes and E8M0 scales (uint8):
+        gate_up [E, I, 2, H/2] / [E, I, 2, H/32], down [E, H, I/2] / [E, H, I/32]. The weights
+        are expanded per GEMM and never trained (LoRA SFT over a released FP4 checkpoint)."""
+        e, i, h = self.num_experts, self.intermediate, self.hidden_size
+        shapes = ((gate_up_fp4, (e, i, 2, h // 2)), (gate_up_scale, (e, i, 2, h // 32)),
+                  (down_fp4, (e, h, i // 2)), (down_scale, (e, h, i // 32)))
+        if any(t.dtype != torch.uint8 or tuple(t.shape) != s for t, s in shapes):
+            raise ValueError("frozen FP4 experts need uint8 codes and scales of the expert shapes")
+        del self.gate_up, self.down
+        for name, (t, _) in zip(("gate_up_fp4", "gate_up_scale", "down_fp4", "down_scale"), shapes):
+            self.register_buffer(name, t)
 
     def forward(self, x, indices, weights):
         batch = self.dispatcher.dispatch(x, indices, weights)
         row_weights = self.dispatcher.row_weights(batch)
-        w1 = self.gate_up.reshape(self.num_experts, 2 * self.intermediate, self.hidden_size)
-        gate_up = ops.grouped_linear(batch.rows, w1, batch.offsets, batch.sizes)
+        if self.frozen_fp4:
+            e, i, h = self.num_experts, self.intermediate, self.hidden_size
+            gate_up = ops.fp4_grouped_linear(batch.rows, self.gate_up_fp4.view(e, 2 * i, h // 2),
+                                             self.gate_up_scale.view(e, 2 * i, h // 32), batch.offsets, batch.sizes,
+                                             2 * i)
+        else:
+            w1 = self.gate_up.reshape(self.num_experts, 2 * self.intermediate, self.hidden_size)
+            gate_up = ops.grouped_linear(batch.rows, w1, batch.offsets, batch.sizes)
         hidden = ops.swiglu(gate_up, row_weights, interleaved=True, limit=self.limit, total=batch.total)
-        out = ops.grouped_linear(hidden, self.down, batch.offsets, batch.sizes)
+        if self.frozen_fp4:
+            out = ops.fp4_grouped_linear(hidden, self.down_fp4, self.down_scale, batch.offsets, batch.sizes,
+                                         self.hidden_size)
+        else:
+            out = ops.grouped_linear(hidden, self.down, batch.offsets, batch.sizes)
         return self.dispatcher.combine(out, batch, weighted=False)
 
 

@@ -3,6 +3,7 @@ CPU tensors run the plain-PyTorch restatement used as the test oracle."""
 
 from ._ext import available, check_status, ext, on_gpu
 from .attention import causal_attention
+from .fp4 import dequantize_fp4, fp4_grouped_linear
 from .gemm import grouped_linear, linear, matmul_nt
 from .loss import linear_cross_entropy, token_log_probs
 from .moe import Routing, build_routing, combine, gather, swiglu
@@ -13,6 +14,6 @@ from .router import AuxGradient, route
 
 __all__ = [
     "AuxGradient", "Routing", "available", "build_routing", "causal_attention", "check_status", "combine",
-    "ext", "gather", "grouped_linear", "inv_freq", "linear", "linear_cross_entropy", "matmul_nt", "on_gpu",
+    "dequantize_fp4", "ext", "fp4_grouped_linear", "gather", "grouped_linear", "inv_freq", "linear", "linear_cross_entropy", "matmul_nt", "on_gpu",
     "qk_norm_rope", "rms_norm", "rope_interleaved", "route", "swiglu", "token_log_probs",
 ]

@@ -62,6 +62,8 @@ def parse_args(argv=None):
     p.add_argument("--lora-targets", help="comma-separated layer-relative linear module suffixes")
     p.add_argument("--engram-offload", action="store_true", help="keep DSV4 Engram rows in host memory")
     p.add_argument("--train-engram", action="store_true", help="also update Engram tables in LoRA mode (SGD)")
+    p.add_argument("--fp4-experts", action="store_true",
+                   help="DSV4 LoRA: keep the frozen routed experts as MXFP4 codes, expanded per GEMM")
     p.add_argument("--gradient-checkpointing", action="store_true")
     p.add_argument("--seed", type=int, default=42)
     p.add_argument("--eval-batches", type=int, default=1, help="fixed evaluation batches per data group")
@@ -88,6 +90,8 @@ def validate_args(args, world_size: int) -> None:
         raise ValueError("cp-size and ep-size must divide world size")
     if args.family != "dsv4" and (args.engram_offload or args.train_engram):
         raise ValueError("Engram options require the DSV4 model family")
+    if args.fp4_experts and (args.family != "dsv4" or args.mode != "lora"):
+        raise ValueError("fp4-experts keeps experts frozen: it requires DSV4 LoRA")
     if args.seq_len % args.cp_size:
         raise ValueError("seq-len must divide evenly across cp-size")
     for name in ("config.json", "model.safetensors.index.json"):
@@ -156,7 +160,7 @@ def load_model(args, runtime):
             args.model_path, num_layers=args.num_layers, device=runtime.device, dtype=dtype, context_parallel=cp,
             token_dispatcher=dispatcher, engram_mesh=meshes.engram if meshes is not None else None,
             sparse_engram_gradients=args.mode == "lora" or args.optimizer == "sgd",
-            engram_offload=args.engram_offload)
+            engram_offload=args.engram_offload, fp4_experts=args.fp4_experts)
         for layer in model.model.layers:
             if layer.attention.indexer is not None:
                 layer.attention.indexer.stable_topk = True
