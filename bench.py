@@ -28,8 +28,8 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "SFT tokens/sec/box (max over ranks)"
 MODEL = "Qwen3-30B-A3B-shaped (48L, H2048, 32q/4kv x128, 128 experts top-8, I768, V151936)"
-# The reference publishes no B200 or Qwen number; the only published SFT throughput is DSV4-Flash
-# on 8x B300, which is a different model, so vs_baseline stays null.
+# The reference publishes no B200 or Qwen number; its only published SFT throughput is for
+# DeepSeek-V4.1-Flash on 8x B300 (docs/testing.md there), a different model, so vs_baseline stays null.
 BASELINE_VALUE = None
 
 
