@@ -1,8 +1,9 @@
 """Causal GQA attention for Qwen3 (``dsv41_train/models/qwen/model.py:84-171``).
 
 Layout: q [B, L, Hq, D], k/v [B, L, Hkv, D] (the token-major layout the QKV kernel writes).
-This entry point currently runs PyTorch's scaled-dot-product attention (a library kernel,
-cuDNN/flash on B200); the own tcgen05 attention kernel replaces it behind the same signature.
+This entry point runs PyTorch's scaled-dot-product attention (a library kernel: cuDNN's fused
+attention on B200). No attention kernel of this library exists yet; every model calls attention
+through this function so one can replace it in a single place.
 """
 
 from __future__ import annotations
