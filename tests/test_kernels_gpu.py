@@ -375,3 +375,31 @@ def test_frozen_fp4_grouped_linear_grad():
     yr.backward(g.float())
     assert _rel(y, yr) < 1e-2
     assert _rel(x.grad, xr.grad) < 1e-2
+
+
+def test_bitwise_determinism_30_runs():
+    """Fixed-order reductions: repeated launches give identical bits (combine, RMSNorm weight
+    gradient, grouped weight-gradient GEMM, routing plan)."""
+    torch.manual_seed(16)
+    t, k, e, h = 700, 8, 16, 512
+    ids = torch.randint(0, e, (t, k), dtype=torch.int32, device=DEV)
+    routing = M.build_routing(ids, e)
+    rows = torch.randn(routing.capacity, h, device=DEV, dtype=torch.bfloat16)
+    w = torch.rand(t, k, device=DEV)
+    x = torch.randn(t, h, device=DEV, dtype=torch.bfloat16)
+    nw = torch.ones(h, device=DEV, dtype=torch.bfloat16)
+    dy = torch.randn_like(x)
+    _, rstd = ops.ext().rmsnorm_fwd(x, nw, 1e-6)
+    gu = torch.randn(routing.capacity, 256, device=DEV, dtype=torch.bfloat16)
+    first = None
+    for _ in range(30):
+        r = M.build_routing(ids, e)
+        out = ops.ext().moe_combine(rows, r.route_rows, w)
+        _, dw = ops.ext().rmsnorm_bwd(dy, x, nw, rstd, True)
+        gw = torch.empty(e, 256, h, device=DEV, dtype=torch.bfloat16)
+        ops.ext().grouped_gemm_k(gu, rows, r.offsets, r.rows, gw, False)
+        cur = (r.route_rows.clone(), out.clone(), dw.clone(), gw.clone())
+        if first is None:
+            first = cur
+        else:
+            assert all(torch.equal(a, b) for a, b in zip(first, cur))
