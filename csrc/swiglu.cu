@@ -114,9 +114,6 @@ __device__ __forceinline__ void load_gu8(const __nv_bfloat16* row, int c, int in
 __global__ void swiglu_fwd_vec_kernel(const __nv_bfloat16* __restrict__ gu, const float* __restrict__ w,
                                       __nv_bfloat16* __restrict__ out, int64_t rows, int inter, bool interleaved,
                                       float limit, const int32_t* __restrict__ row_limit) {
-  // Each lane handles up to kChunks 8-column chunks of a row; all of a lane's loads are issued
-  // before any math so several 16-byte requests are in flight per lane.
-  constexpr int kChunks = 4;
   const int lane = threadIdx.x & 31;
   const int64_t live = row_limit != nullptr ? min(rows, static_cast<int64_t>(*row_limit)) : rows;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
@@ -124,30 +121,20 @@ __global__ void swiglu_fwd_vec_kernel(const __nv_bfloat16* __restrict__ gu, cons
        row += warps) {
     const float ws = w != nullptr ? w[row] : 1.f;
     const __nv_bfloat16* src = gu + row * 2 * inter;
-    for (int c0 = lane * 8; c0 < inter; c0 += 256 * kChunks) {
-      float g[kChunks][8], u[kChunks][8];
+    for (int c = lane * 8; c < inter; c += 256) {
+      float g[8], u[8], o[8];
+      load_gu8(src, c, inter, interleaved, g, u);
 #pragma unroll
-      for (int j = 0; j < kChunks; ++j) {
-        const int c = c0 + j * 256;
-        if (c < inter) load_gu8(src, c, inter, interleaved, g[j], u[j]);
-      }
-#pragma unroll
-      for (int j = 0; j < kChunks; ++j) {
-        const int c = c0 + j * 256;
-        if (c >= inter) break;
-        float o[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          float gg = g[j][i], uu = u[j][i];
-          if (limit > 0.f) {
-            gg = fminf(gg, limit);
-            uu = fminf(fmaxf(uu, -limit), limit);
-          }
-          const float sv = (gg == -INFINITY) ? 0.f : silu_f(gg);
-          o[i] = sv * uu * ws;
+      for (int i = 0; i < 8; ++i) {
+        float gg = g[i], uu = u[i];
+        if (limit > 0.f) {
+          gg = fminf(gg, limit);
+          uu = fminf(fmaxf(uu, -limit), limit);
         }
-        store_bf16x8(out + row * inter + c, o);
+        const float sv = (gg == -INFINITY) ? 0.f : silu_f(gg);
+        o[i] = sv * uu * ws;
       }
+      store_bf16x8(out + row * inter + c, o);
     }
   }
 }
