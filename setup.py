@@ -43,7 +43,16 @@ if os.environ.get("TDSV_BOUNDS_CHECK"):
 setup(
     name="tiny_dsv41_b200",
     version="0.1.0",
-    packages=["tiny_dsv41_b200"],
+    packages=["tiny_dsv41_b200", "tiny_dsv41_b200.models", "tiny_dsv41_b200.models.dsv4",
+              "tiny_dsv41_b200.models.qwen", "tiny_dsv41_b200.ops", "tiny_dsv41_b200.optim",
+              "tiny_dsv41_b200.parallel", "tiny_dsv41_b200.rl", "tiny_dsv41_b200.rollout", "tiny_dsv41_b200.train",
+              "tiny_dsv41_b200.utils"],
+    package_data={"tiny_dsv41_b200.models.dsv4": ["tiny_config.json"]},
+    entry_points={"console_scripts": [
+        "rollout-manager = tiny_dsv41_b200.rollout.cli:main",
+        "tdsv-rl-train = tiny_dsv41_b200.rl.train:main",
+        "tdsv-sft = tiny_dsv41_b200.train.sft:main",
+    ]},
     ext_modules=[
         CUDAExtension(
             name="tiny_dsv41_b200._C",
