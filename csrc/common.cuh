@@ -333,6 +333,14 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int m, int n, bool a_mn_m
          ((static_cast<uint32_t>(n) >> 3) << 17) | ((static_cast<uint32_t>(m) >> 4) << 24);
 }
 
+// Host helpers defined in gemm_tc.cu: the driver's cuTensorMapEncodeTiled (resolved once through
+// the runtime, so nothing links libcuda) and binding the device's primary context to this thread.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn();
+void bind_primary_context();
+
 inline int num_sms() {
   static int n = [] {
     int dev = 0, v = 0;

@@ -342,13 +342,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+}  // namespace
+
 // ---------------------------------------------------------------------------------------------
 // Host side: tensor maps through the driver entry point (no libcuda link dependency).
 // ---------------------------------------------------------------------------------------------
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
 EncodeTiledFn encode_fn() {
   static EncodeTiledFn fn = [] {
     void* ptr = nullptr;
@@ -372,6 +370,8 @@ void bind_primary_context() {
     bound_device = dev;
   }
 }
+
+namespace {
 
 // Row-major tensor [outer..., rows, inner] with a box of {box_inner, box_rows, 1...}, 128B swizzle.
 CUtensorMap make_map(const at::Tensor& t, int box_rows, int box_inner = 64) {
