@@ -7,7 +7,8 @@
 Each case times its kernel with CUDA events on the launching stream after warm-up (inputs are
 larger than the 126 MB L2 unless noted) and reports achieved TFLOP/s or GB/s and the fraction of
 ``MEASURED_PEAKS.json`` (cuBLAS bf16 burst / copy bandwidth measured on this hardware); GEMM
-cases also time ``torch.matmul`` (cuBLAS) on the same operands.
+cases also time ``torch.matmul`` (cuBLAS) on the same operands, attention cases PyTorch's
+scaled-dot-product attention (cuDNN on B200) on the same q / k / v.
 """
 
 from __future__ import annotations
@@ -91,6 +92,29 @@ def cases():
         w = torch.ones(h, device=dev, dtype=bf)
         return (lambda: C.rmsnorm_fwd(x, w, 1e-6)), None, None, rows * h * 2 * 2
 
+    def attention(kind, batch=1, seq=4096, heads=32, kv_heads=4):
+        # Qwen3-30B-A3B attention shape; causal FLOPs = half of the dense 4 * B * H * L^2 * D
+        import torch.nn.functional as F
+
+        q = torch.randn(batch, seq, heads, 128, device=dev, dtype=bf)
+        k = torch.randn(batch, seq, kv_heads, 128, device=dev, dtype=bf)
+        v = torch.randn(batch, seq, kv_heads, 128, device=dev, dtype=bf)
+        fwd_flops = 2 * batch * heads * seq * seq * 128
+        qh, kh, vh = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+        if kind == "fwd":
+            def sdpa():
+                return F.scaled_dot_product_attention(qh, kh, vh, is_causal=True, enable_gqa=True)
+            return (lambda: C.attn_fwd(q, k, v)), sdpa, fwd_flops, None
+        out, lse = C.attn_fwd(q, k, v)
+        dout = torch.randn_like(q)
+        qr, kr, vr = (t.detach().requires_grad_() for t in (qh, kh, vh))
+        ref_out = F.scaled_dot_product_attention(qr, kr, vr, is_causal=True, enable_gqa=True)
+        dref = dout.transpose(1, 2)
+
+        def sdpa_bwd():
+            return torch.autograd.grad(ref_out, (qr, kr, vr), dref, retain_graph=True)
+        return (lambda: C.attn_bwd(dout, q, k, v, out, lse)), sdpa_bwd, int(2.5 * fwd_flops), None
+
     return {
         "dense_lm_head": lambda: dense(4096, 151936, 2048),
         "dense_qkv": lambda: dense(4096, 5120, 2048),
@@ -101,6 +125,8 @@ def cases():
         "adamw": adamw,
         "swiglu": swiglu,
         "rmsnorm": rmsnorm,
+        "attn_fwd": lambda: attention("fwd"),
+        "attn_bwd": lambda: attention("bwd"),
     }
 
 
@@ -130,7 +156,8 @@ def main(argv=None) -> None:
             row.update(gbs=round(nbytes / ms / 1e6, 1), frac_of_peak=round(nbytes / ms / 1e6 / peaks["gbs"], 3))
         if ref is not None:
             rms = _time(ref, args.iters)
-            row.update(cublas_ms=round(rms, 4), cublas_tflops=round(flops / rms / 1e9, 1))
+            label = "cudnn_sdpa" if name.startswith("attn") else "cublas"
+            row.update({f"{label}_ms": round(rms, 4), f"{label}_tflops": round(flops / rms / 1e9, 1)})
         row["peak_source"] = peaks["source"]
         print(json.dumps(row), flush=True)
         del fn, ref
