@@ -113,8 +113,13 @@ void ep_combine_push(const at::Tensor& y, const at::Tensor& route, const c10::op
                      const at::Tensor& peer_flags, int64_t my_rank, int64_t epoch);
 at::Tensor ep_reduce_returned(const at::Tensor& ret, const at::Tensor& dest_mask, const at::Tensor& slot,
                               int64_t tokens);
+// index_scores.cu
+at::Tensor index_scores(const at::Tensor& query, const at::Tensor& keys, const at::Tensor& weights,
+                        const at::Tensor& starts, const at::Tensor& ends, int64_t width,
+                        const c10::optional<at::Tensor>& candidates);
 // attention.cu
-std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v);
+std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                                 const c10::optional<at::Tensor>& trace);
 std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                  const at::Tensor& v, const at::Tensor& out, const at::Tensor& lse);
 }  // namespace tdsv
@@ -127,8 +132,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ids"), py::arg("num_experts"), py::arg("block") = 128, py::arg("slab_counts") = py::none(),
         py::arg("slab") = 1);
   m.def("ep_dest_plan", &tdsv::ep_dest_plan, "per-token destination ranks, receive slots and counts");
-  m.def("attn_fwd", &tdsv::attn_fwd, "causal GQA flash attention forward (tcgen05): (out, lse)");
+  m.def("attn_fwd", &tdsv::attn_fwd, "causal GQA flash attention forward (tcgen05): (out, lse)", py::arg("q"),
+        py::arg("k"), py::arg("v"), py::arg("trace") = py::none());
   m.def("attn_bwd", &tdsv::attn_bwd, "causal GQA flash attention backward (tcgen05): (dq, dk, dv)");
+  m.def("index_scores", &tdsv::index_scores, "DSV4 sparse-indexer scores (tcgen05, fused relu / head reduction)");
   m.def("fp4_dequant", &tdsv::fp4_dequant, "MXFP4 (E2M1 + E8M0 per 32) to bf16");
   m.def("rmsnorm_fwd", &tdsv::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &tdsv::rmsnorm_bwd);

@@ -10,15 +10,19 @@ K1/K2 kernels of ``sparse_attention.py``).
 ``index_scores`` = sum_h w[q,h] * relu(q_h . k) * d^-1/2 over each query's visible compressed
 keys (``sparse_indexer.py:156-172``), -inf outside [start, end) or outside the candidate mask.
 
-Both are written as gathered batched matmuls (cuBLAS through PyTorch) in this module; the
-tcgen05 kernels for the 64-head x 512-dim MQA tile are a planned replacement behind the same
-signatures.
+On CUDA, ``index_scores`` runs the tcgen05 kernel of ``csrc/index_scores.cu`` (keys as the M
+operand, the block's (query, head) rows as N, relu / head weights / head reduction in the TMEM
+epilogue; head dim 64 or 128, heads a power of two). ``sparse_attention`` is a gathered batched
+matmul (cuBLAS through PyTorch); its own kernel is not built yet. The PyTorch restatements below
+are the oracle on CPU.
 """
 
 from __future__ import annotations
 
 import torch
 import torch.nn.functional as F
+
+from ._ext import ext, on_gpu
 
 
 def sparse_attention(query, kv, window_indices, window_mask, compressed_kv, compressed_indices, sinks, *,
@@ -48,7 +52,23 @@ def sparse_attention(query, kv, window_indices, window_mask, compressed_kv, comp
     return out.transpose(1, 2).contiguous()
 
 
+def _index_kernel_ok(query, keys, weights, width, candidates) -> bool:
+    heads, dim = query.shape[2], query.shape[3]
+    return (query.dtype == torch.bfloat16 and keys.dtype == torch.bfloat16 and dim in (64, 128)
+            and 1 <= heads <= 128 and heads & (heads - 1) == 0 and width > 0
+            and (candidates is None or candidates.numel() == query.shape[0] * query.shape[1] * width))
+
+
 def index_scores(query, keys, weights, starts, ends, width, candidates=None):
+    if on_gpu(query) and _index_kernel_ok(query, keys, weights, width, candidates):
+        cand = None if candidates is None else candidates.bool().contiguous()
+        return ext().index_scores(query.contiguous(), keys.contiguous(), weights.float().contiguous(),
+                                  starts.to(torch.int32).contiguous(), ends.to(torch.int32).contiguous(),
+                                  int(width), cand)
+    return index_scores_reference(query, keys, weights, starts, ends, width, candidates)
+
+
+def index_scores_reference(query, keys, weights, starts, ends, width, candidates=None):
     if width == 0:
         return query.new_empty((*query.shape[:2], 0), dtype=torch.float32)
     idx = starts.unsqueeze(-1) + torch.arange(width, device=query.device)
@@ -62,4 +82,4 @@ def index_scores(query, keys, weights, starts, ends, width, candidates=None):
     return scores.masked_fill(~valid, float("-inf"))
 
 
-__all__ = ["index_scores", "sparse_attention"]
+__all__ = ["index_scores", "index_scores_reference", "sparse_attention"]
