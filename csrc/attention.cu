@@ -23,15 +23,16 @@
 //   (TMA warp, MMA warp, 8 compute warps: two per key row, each owning 32 of the 64 queries).
 //   S^T = K Q^T and dP^T = V dO^T put one key per TMEM lane, so the thread that owns key row r
 //   computes P^T = exp2(S^T c - lse2) and dS^T = P^T (dP^T - D) for its row and stores both as
-//   bf16 back over its own S / dP columns: dV += P^T dO and dK += dS^T Q take them from tensor
+//   bf16 back over its own S columns: dV += P^T dO and dK += dS^T Q take them from tensor
 //   memory as the A operand (accumulated in TMEM over the whole loop). dS^T also goes to shared
 //   memory as the B operand of dQ^T = K^T dS^T (fresh per block); the thread owning head dim r
 //   adds its dQ^T row into an fp32 [B, L, H, 128] buffer with coalesced reductions (a warp covers
 //   32 adjacent dims). D = rowsum(dO * O) and lse2 = lse log2(e) come from a small prep kernel;
 //   dK / dV of the query heads of one GQA group meet in fp32 buffers (TMA reduce-add) and a
 //   finalize kernel scales and converts dQ / dK / dV to bf16.
-//   Issue order per block i: [P_i, dS_i ready] dV_i, dK_i, dQ_i, dP_{i+1}, S_{i+2}; the softmax of
-//   block i+1 (on S_{i+1}, issued a block earlier) overlaps the dV / dK / dQ MMAs of block i.
+//   Issue order per block i: [dP_i read] dP_{i+1}, [P_i, dS_i ready] dV_i, dK_i, dQ_i, S_{i+2}: the
+//   compute warps of block i+1 find S_{i+1} and dP_{i+1} ready while the tensor cores work on the
+//   dV / dK / dQ of block i (dS^T is double-buffered in shared memory).
 //   TMEM: S0 [0, 64), S1 [64, 128), dP [128, 192), dQ^T [192, 256), dV [256, 384), dK [384, 512).
 //
 // No reference counterpart: the reference runs torch's scaled_dot_product_attention
@@ -56,9 +57,17 @@ constexpr float kLog2e = 1.4426950408889634f;
 enum : int {
   kFwdWaitKvEmpty = 301, kFwdWaitQ, kFwdWaitKv0, kFwdWaitKv, kFwdWaitSFree, kFwdWaitP, kFwdWaitS, kFwdWaitPV,
   kFwdWaitLast, kFwdWaitPair,
-  kBwdWaitQEmpty = 321, kBwdWaitKv, kBwdWaitQ, kBwdWaitPds, kBwdWaitDqFree,
+  kBwdWaitQEmpty = 321, kBwdWaitKv, kBwdWaitQ, kBwdWaitDpFree, kBwdWaitPds, kBwdWaitDqFree, kBwdWaitGroup,
   kBwdWaitS, kBwdWaitDp, kBwdWaitPdsFree, kBwdWaitDq, kBwdWaitQc,
 };
+
+// Optional per-CTA event timeline (a diagnostic for pipeline tuning): with a non-null `trace`,
+// CTA (0, 0, 0) records the SM clock, relative to its entry, of event e at iteration i in
+// trace[e * 64 + i]. Needs `tracing`, `trace` and `t0` in scope.
+#define TDSV_TRACE(event, it)                                              \
+  do {                                                                     \
+    if (tracing && (it) < 64) trace[(event) * 64 + (it)] = clock64() - t0; \
+  } while (0)
 
 // =============================================================================================
 // Forward
@@ -94,10 +103,6 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
   // optional event timeline of CTA (0, 0, 0): trace[event * 64 + iteration] = SM clock since entry
   const long long t0 = clock64();
   const bool tracing = trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
-#define TDSV_TRACE(event, it)                                            \
-  do {                                                                   \
-    if (tracing && (it) < 64) trace[(event) * 64 + (it)] = clock64() - t0; \
-  } while (0)
   extern __shared__ uint8_t smem_raw[];
   FwdSmem& sm = *reinterpret_cast<FwdSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -147,12 +152,12 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
       for (int j = 0; j < n_kv; ++j) {
         const int s = j & 1;
         const int key0 = b * seq + j * kTile;
-        if (j >= 2 && !mbar_wait(&sm.k_empty[s], ((j >> 1) - 1) & 1, status, kFwdWaitKvEmpty)) break;
+        if (j >= 2 && !mbar_sleep_wait(&sm.k_empty[s], ((j >> 1) - 1) & 1, status, kFwdWaitKvEmpty)) break;
         mbar_arrive_expect_tx(&sm.k_full[s], 2 * kAtom);
         tma_load_3d(sm.k[s], &tk, &sm.k_full[s], 0, hk, key0);
         tma_load_3d(sm.k[s] + kAtom, &tk, &sm.k_full[s], 64, hk, key0);
         TDSV_TRACE(0, j);
-        if (j >= 2 && !mbar_wait(&sm.v_empty[s], ((j >> 1) - 1) & 1, status, kFwdWaitKvEmpty)) break;
+        if (j >= 2 && !mbar_sleep_wait(&sm.v_empty[s], ((j >> 1) - 1) & 1, status, kFwdWaitKvEmpty)) break;
         mbar_arrive_expect_tx(&sm.v_full[s], 2 * kAtom);
         tma_load_3d(sm.v[s], &tv, &sm.v_full[s], 0, hk, key0);
         tma_load_3d(sm.v[s] + kAtom, &tv, &sm.v_full[s], 64, hk, key0);
@@ -165,7 +170,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
       const uint32_t idesc_pv = make_idesc_bf16(kTile, kDim, false, true);
       // Q (bf16, 64 packed columns at kColQ) is the A operand of every S MMA, read from TMEM
       auto q_col = [&](int kk) { return tmem + kFwdColQ + (kk >> 2) * 32 + (kk & 3) * 8; };
-      bool ok = mbar_wait(&sm.q_tmem, 0, status, kFwdWaitQ) && mbar_wait(&sm.k_full[0], 0, status, kFwdWaitKv0);
+      bool ok = mbar_sleep_wait(&sm.q_tmem, 0, status, kFwdWaitQ) && mbar_sleep_wait(&sm.k_full[0], 0, status, kFwdWaitKv0);
       if (ok) {
         tc_fence_after();
         const uint32_t ka = smem_u32(sm.k[0]);
@@ -179,8 +184,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
       for (int j = 0; ok && j < n_kv; ++j) {
         if (j + 1 < n_kv) {
           const int sn = (j + 1) & 1;
-          ok = mbar_wait(&sm.k_full[sn], ((j + 1) >> 1) & 1, status, kFwdWaitKv);
-          if (ok && j + 1 >= 2) ok = mbar_wait(&sm.s_free[sn], (((j + 1) >> 1) - 1) & 1, status, kFwdWaitSFree);
+          ok = mbar_sleep_wait(&sm.k_full[sn], ((j + 1) >> 1) & 1, status, kFwdWaitKv);
+          if (ok && j + 1 >= 2) ok = mbar_sleep_wait(&sm.s_free[sn], (((j + 1) >> 1) - 1) & 1, status, kFwdWaitSFree);
           if (!ok) break;
           tc_fence_after();
           const uint32_t ka = smem_u32(sm.k[sn]);
@@ -191,9 +196,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
           umma_commit(&sm.k_empty[sn]);
           TDSV_TRACE(2, j + 1);
         }
-        if (!(ok = mbar_wait(&sm.p_full, j & 1, status, kFwdWaitP))) break;
+        if (!(ok = mbar_sleep_wait(&sm.p_full, j & 1, status, kFwdWaitP))) break;
         TDSV_TRACE(3, j);
-        if (!(ok = mbar_wait(&sm.v_full[j & 1], (j >> 1) & 1, status, kFwdWaitKv))) break;
+        if (!(ok = mbar_sleep_wait(&sm.v_full[j & 1], (j >> 1) & 1, status, kFwdWaitKv))) break;
         tc_fence_after();
         const uint32_t va = smem_u32(sm.v[j & 1]);
         // P_j sits in S_j's TMEM columns: keys [64 h, 64 h + 64) as 32 packed bf16x2 words at
@@ -286,18 +291,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
           const float p0 = ex2_approx(fmaf(__uint_as_float(sv[c][i]), scale_log2, -m_used));
           const float p1 = ex2_approx(fmaf(__uint_as_float(sv[c][i + 1]), scale_log2, -m_used));
           const __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-          // the row sum adds exactly what the PV MMA multiplies (the bf16-rounded P)
-          s8[(i >> 1) & 7] += __low2float(pb) + __high2float(pb);
+          s8[(i >> 1) & 7] += p0 + p1;
           packed[c * 16 + i / 2] = *reinterpret_cast<const uint32_t*>(&pb);
         }
       l = l * alpha + (((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])));
-      if (tr_lane) TDSV_TRACE(8, j);
-      if (j > 0) {
-        // PV_{j-1} complete: O may be rescaled and P overwritten
+      // P_j goes to the other S buffer than P_{j-1}, so only a rescale of O has to wait for PV_{j-1}
+      // (no phase of pv_done can complete twice meanwhile: PV_j needs this thread's P_j first)
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
         if (!(ok = warp_wait(&sm.pv_done, (j - 1) & 1, status, kFwdWaitPV))) break;
-        if (tr_lane) TDSV_TRACE(9, j);
         tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha != 1.f)) {
+        {
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             uint32_t ov[32];
@@ -316,8 +319,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&sm.p_full);
-      if (tr_lane) TDSV_TRACE(10, j);
-      if (lane == 0 && warp == 6) TDSV_TRACE(11, j);
+      if (lane == 0) TDSV_TRACE(6 + warp, j);  // events 8..15: p_full arrival of warps 2..9
     }
     if (ok) {  // the two halves of each row add their partial sums
       sm.xchg[n_kv & 1][half][r] = l;
@@ -353,29 +355,32 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
     __syncwarp();
     tmem_dealloc(tmem, 512);
   }
-#undef TDSV_TRACE
 }
 
 // =============================================================================================
 // Backward
 // =============================================================================================
+constexpr int kQStages = 3;  // Q / dO / lse2 / D ring of the backward: block i + 2 loads while block i computes
+
 struct BwdSmem {
   alignas(1024) uint8_t k[2 * kAtom];           // [128 keys x 128 dims]
   alignas(1024) uint8_t v[2 * kAtom];
-  alignas(1024) uint8_t q[2][2 * kHalfAtom];    // per stage [64 queries x 128 dims]; reduce staging at the end
-  alignas(1024) uint8_t dout[2][2 * kHalfAtom];
-  alignas(1024) uint8_t dst[kAtom];             // dS^T [128 keys x 64 queries]: B operand of the dQ^T MMA
-  alignas(16) float lse2[2][kQBlk];
-  alignas(16) float dvec[2][kQBlk];
+  alignas(1024) uint8_t q[kQStages][2 * kHalfAtom];  // per stage [64 queries x 128 dims]; reduce staging at the end
+  alignas(1024) uint8_t dout[kQStages][2 * kHalfAtom];
+  alignas(1024) uint8_t dst[2][kAtom];          // dS^T [128 keys x 64 queries] per block parity: B of the dQ^T MMA
+  alignas(16) float lse2[kQStages][kQBlk];
+  alignas(16) float dvec[kQStages][kQBlk];
   uint64_t kv_full;
-  uint64_t q_full[2];
-  uint64_t q_empty[2];
+  uint64_t q_full[kQStages];
+  uint64_t q_empty[kQStages];
   uint64_t s_full[2];
   uint64_t dp_full;
+  uint64_t dp_free;  // the compute warps have read dP^T
   uint64_t pds_ready;
-  uint64_t pds_free;
+  uint64_t pds_free[2];  // per dS^T shared-memory buffer: its dQ^T MMA is done
   uint64_t dq_full;
   uint64_t dq_free;
+  uint64_t grp[2];  // completion of MMA groups (alternating), to bound how many are queued
   uint32_t tmem_base;
 };
 
@@ -405,13 +410,16 @@ __device__ __forceinline__ void drain_reduce(uint32_t taddr, int chunks, uint8_t
 }
 
 constexpr int kBwdThreads = 320;  // TMA warp, MMA warp, 8 compute warps
+constexpr int kBwdLoadWarp = 1, kBwdMmaWarp = 0;
 
 __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(
     const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
     const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
     const __grid_constant__ CUtensorMap tdk_acc, const __grid_constant__ CUtensorMap tdv_acc,
     float* __restrict__ dq_acc, const float* __restrict__ lse2, const float* __restrict__ dvec, int seq, int heads,
-    int kv_heads, float scale_log2, int* __restrict__ status) {
+    int kv_heads, float scale_log2, int* __restrict__ status, long long* __restrict__ trace) {
+  const long long t0 = clock64();
+  const bool tracing = trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
   extern __shared__ uint8_t smem_raw[];
   BwdSmem& sm = *reinterpret_cast<BwdSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -426,16 +434,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kQStages; ++s) {
       mbar_init(&sm.q_full[s], 1);
       mbar_init(&sm.q_empty[s], 1);
-      mbar_init(&sm.s_full[s], 1);
     }
+    for (int s = 0; s < 2; ++s) mbar_init(&sm.s_full[s], 1);
     mbar_init(&sm.dp_full, 1);
+    mbar_init(&sm.dp_free, 256);
     mbar_init(&sm.pds_ready, 256);
-    mbar_init(&sm.pds_free, 1);
+    mbar_init(&sm.pds_free[0], 1);
+    mbar_init(&sm.pds_free[1], 1);
     mbar_init(&sm.dq_full, 1);
     mbar_init(&sm.dq_free, 256);
+    mbar_init(&sm.grp[0], 1);
+    mbar_init(&sm.grp[1], 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -447,7 +459,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
 
-  if (warp == 0) {
+  if (warp == kBwdLoadWarp) {
     if (elect_one()) {
       tma_prefetch_desc(&tq);
       tma_prefetch_desc(&tk);
@@ -459,8 +471,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(
       tma_load_3d(sm.v, &tv, &sm.kv_full, 0, hk, key0);
       tma_load_3d(sm.v + kAtom, &tv, &sm.kv_full, 64, hk, key0);
       for (int it = 0; it < n_it; ++it) {
-        const int s = it & 1;
-        if (it >= 2 && !mbar_wait(&sm.q_empty[s], ((it >> 1) - 1) & 1, status, kBwdWaitQEmpty)) break;
+        const int s = it % kQStages;
+        if (it >= kQStages && !mbar_sleep_wait(&sm.q_empty[s], ((it / kQStages) - 1) & 1, status, kBwdWaitQEmpty)) break;
         const int qrow = b * seq + (i0 + it) * kQBlk;
         mbar_arrive_expect_tx(&sm.q_full[s], 4 * kHalfAtom + 2 * kQBlk * 4);
         tma_load_3d(sm.q[s], &tq, &sm.q_full[s], 0, h, qrow);
@@ -472,65 +484,90 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(
         bulk_load_1d(sm.dvec[s], dvec + off, kQBlk * 4, &sm.q_full[s]);
       }
     }
-  } else if (warp == 1) {
+  } else if (warp == kBwdMmaWarp) {
     if (elect_one()) {
       const uint32_t idesc_sp = make_idesc_bf16(kTile, kQBlk, false, false);  // S^T, dP^T: M keys, N queries
       const uint32_t idesc_kv = make_idesc_bf16(kTile, kDim, false, true);    // dV, dK: M keys, N dims
       const uint32_t idesc_q = make_idesc_bf16(kDim, kQBlk, true, true);      // dQ^T: M dims, N queries
-      const uint32_t ka = smem_u32(sm.k), va = smem_u32(sm.v), dsa = smem_u32(sm.dst);
+      const uint32_t ka = smem_u32(sm.k), va = smem_u32(sm.v);
+      // At most two groups of MMAs are queued: the issuing thread shares a scheduler with two
+      // compute warps, and an MMA that waits for queue space holds that scheduler's issue slot.
+      uint32_t groups = 0;
+      auto open_group = [&]() {
+        return groups < 2 || mbar_sleep_wait(&sm.grp[groups & 1], ((groups >> 1) - 1) & 1, status, kBwdWaitGroup);
+      };
+      auto close_group = [&]() { umma_commit(&sm.grp[groups++ & 1]); };
       auto issue_s = [&](int it) {  // S^T_it = K Q_it^T into S buffer it & 1
-        const uint32_t qa = smem_u32(sm.q[it & 1]);
+        const uint32_t qa = smem_u32(sm.q[it % kQStages]);
 #pragma unroll
         for (int kk = 0; kk < kDim / 16; ++kk)
           umma_f16(tmem + kColS + (it & 1) * kQBlk, kmajor_desc(ka, kk, kAtom), kmajor_desc(qa, kk, kHalfAtom),
                    idesc_sp, kk > 0);
         umma_commit(&sm.s_full[it & 1]);
+        close_group();
       };
       auto issue_dp = [&](int it) {  // dP^T_it = V dO_it^T
-        const uint32_t doa = smem_u32(sm.dout[it & 1]);
+        const uint32_t doa = smem_u32(sm.dout[it % kQStages]);
 #pragma unroll
         for (int kk = 0; kk < kDim / 16; ++kk)
           umma_f16(tmem + kColDp, kmajor_desc(va, kk, kAtom), kmajor_desc(doa, kk, kHalfAtom), idesc_sp, kk > 0);
         umma_commit(&sm.dp_full);
+        close_group();
       };
-      bool ok = mbar_wait(&sm.kv_full, 0, status, kBwdWaitKv) && mbar_wait(&sm.q_full[0], 0, status, kBwdWaitQ);
+      bool ok = mbar_sleep_wait(&sm.kv_full, 0, status, kBwdWaitKv) && mbar_sleep_wait(&sm.q_full[0], 0, status, kBwdWaitQ);
       if (ok) {
         tc_fence_after();
         issue_s(0);
         issue_dp(0);
       }
-      if (ok && n_it > 1 && (ok = mbar_wait(&sm.q_full[1], 0, status, kBwdWaitQ))) {
+      if (ok && n_it > 1 && (ok = mbar_sleep_wait(&sm.q_full[1], 0, status, kBwdWaitQ) && open_group())) {
         tc_fence_after();
         issue_s(1);
       }
       for (int it = 0; ok && it < n_it; ++it) {
-        const int s = it & 1;
-        // P^T_it (in S buffer s) and dS^T_it (in the dP columns) written to TMEM, dS^T_it to shared memory
-        if (!(ok = mbar_wait(&sm.pds_ready, it & 1, status, kBwdWaitPds))) break;
+        const int s = it & 1, st = it % kQStages;
+        // dP^T_{it+1} as soon as the compute warps have read dP^T_it (dO_{it+1} arrived with Q_{it+1})
+        if (it + 1 < n_it) {
+          if (!(ok = mbar_sleep_wait(&sm.dp_free, it & 1, status, kBwdWaitDpFree) && open_group())) break;
+          tc_fence_after();
+          issue_dp(it + 1);
+        }
+        TDSV_TRACE(4, it);
+        // P^T_it and dS^T_it (bf16, in S buffer s) in TMEM, dS^T_it also in shared memory
+        if (!(ok = mbar_sleep_wait(&sm.pds_ready, it & 1, status, kBwdWaitPds) && open_group())) break;
+        TDSV_TRACE(0, it);
         tc_fence_after();
-        const uint32_t doa = smem_u32(sm.dout[s]), qa = smem_u32(sm.q[s]);
+        const uint32_t doa = smem_u32(sm.dout[st]), qa = smem_u32(sm.q[st]);
 #pragma unroll
         for (int kk = 0; kk < kQBlk / 16; ++kk) {
-          // queries [16 kk, 16 kk + 16): half kk / 2 of the block, 8 packed columns each
-          const uint32_t col = (kk >> 1) * 32 + (kk & 1) * 8;
+          // queries [16 kk, 16 kk + 16): half kk / 2 of the block; each half holds 16 packed columns of
+          // P^T followed by 16 of dS^T
+          const uint32_t col = kColS + s * kQBlk + (kk >> 1) * 32 + (kk & 1) * 8;
           const uint32_t acc = (it > 0 || kk > 0) ? 1u : 0u;
-          umma_f16_ts(tmem + kColDv, tmem + kColS + s * kQBlk + col, mnmajor_desc(doa, kk, kHalfAtom), idesc_kv, acc);
-          umma_f16_ts(tmem + kColDk, tmem + kColDp + col, mnmajor_desc(qa, kk, kHalfAtom), idesc_kv, acc);
+          umma_f16_ts(tmem + kColDv, tmem + col, mnmajor_desc(doa, kk, kHalfAtom), idesc_kv, acc);
+          umma_f16_ts(tmem + kColDk, tmem + col + 16, mnmajor_desc(qa, kk, kHalfAtom), idesc_kv, acc);
         }
-        umma_commit(&sm.q_empty[s]);
+        umma_commit(&sm.q_empty[st]);
+        close_group();
+        TDSV_TRACE(1, it);
         // dQ^T_it = K^T dS^T_it (the previous block's dQ^T must have been drained)
-        if (it >= 1 && !(ok = mbar_wait(&sm.dq_free, (it - 1) & 1, status, kBwdWaitDqFree))) break;
+        if (!(ok = (it == 0 || mbar_sleep_wait(&sm.dq_free, (it - 1) & 1, status, kBwdWaitDqFree)) && open_group())) break;
+        TDSV_TRACE(2, it);
         tc_fence_after();
+        const uint32_t dsa = smem_u32(sm.dst[s]);
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
           umma_f16(tmem + kColDq, mnmajor_desc(ka, kk, kAtom), mnmajor_desc(dsa, kk, kAtom), idesc_q, kk > 0);
         umma_commit(&sm.dq_full);
-        umma_commit(&sm.pds_free);
-        // the next dP^T overwrites dS^T_it and the S^T after next overwrites P^T_it: both were read by
-        // the dV / dK MMAs above, which this thread issued first
-        if (it + 1 < n_it) issue_dp(it + 1);
+        umma_commit(&sm.pds_free[s]);  // dS^T_it in shared memory consumed
+        close_group();
+        TDSV_TRACE(3, it);
+        // S^T_{it+2} overwrites P^T_it / dS^T_it in S buffer s, read by the dV / dK MMAs above (in order)
         if (it + 2 < n_it) {
-          if (!(ok = mbar_wait(&sm.q_full[s], ((it + 2) >> 1) & 1, status, kBwdWaitQ))) break;
+          if (!(ok = mbar_sleep_wait(&sm.q_full[(it + 2) % kQStages], ((it + 2) / kQStages) & 1, status, kBwdWaitQ) &&
+                     open_group()))
+            break;
+          TDSV_TRACE(5, it);
           tc_fence_after();
           issue_s(it + 2);
         }
@@ -558,15 +595,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(
     for (int it = 0; it < n_it; ++it) {
       const int s = it & 1;
       const int q0 = (i0 + it) * kQBlk + half * 32;  // first query of this thread's half
-      if (!(ok = warp_wait(&sm.q_full[s], (it >> 1) & 1, status, kBwdWaitQc))) break;
+      const int st = it % kQStages;
+      if (!(ok = warp_wait(&sm.q_full[st], (it / kQStages) & 1, status, kBwdWaitQc))) break;
       if (!(ok = warp_wait(&sm.s_full[s], (it >> 1) & 1, status, kBwdWaitS))) break;
+      const bool tr_lane = lane == 0 && warp == 2;
+      if (tr_lane) TDSV_TRACE(6, it);
       tc_fence_after();
       uint32_t sv[32];
       tmem_ld_32x32b_x32(lane_addr + kColS + s * kQBlk + half * 32, sv);
       tmem_ld_wait();
       const bool diag = q0 < (j + 1) * kTile;
-      const float* lse_s = sm.lse2[s] + half * 32;
-      const float* d_s = sm.dvec[s] + half * 32;
+      const float* lse_s = sm.lse2[st] + half * 32;
+      const float* d_s = sm.dvec[st] + half * 32;
       float p[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
@@ -582,9 +622,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(
       // P^T (bf16) over this thread's own S columns: the A operand of the dV MMA
       tmem_st_32x32b_x16(lane_addr + kColS + s * kQBlk + half * 32, pk);
       if (!(ok = warp_wait(&sm.dp_full, it & 1, status, kBwdWaitDp))) break;
+      if (tr_lane) TDSV_TRACE(7, it);
       tc_fence_after();
       tmem_ld_32x32b_x32(lane_addr + kColDp + half * 32, sv);
       tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&sm.dp_free);
       uint32_t dk[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -593,18 +636,20 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(
         const __nv_bfloat162 t = __floats2bfloat162_rn(d0, d1);
         dk[i] = *reinterpret_cast<const uint32_t*>(&t);
       }
-      // dS^T over this thread's own dP columns (A operand of the dK MMA) and into shared memory
-      // (B operand of the dQ^T MMA, once the previous dQ^T MMA has read it)
-      tmem_st_32x32b_x16(lane_addr + kColDp + half * 32, dk);
-      if (it >= 1 && !(ok = warp_wait(&sm.pds_free, (it - 1) & 1, status, kBwdWaitPdsFree))) break;
+      // dS^T next to P^T in this thread's own S columns (A operand of the dK MMA) and into shared
+      // memory (B operand of the dQ^T MMA)
+      tmem_st_32x32b_x16(lane_addr + kColS + s * kQBlk + half * 32 + 16, dk);
+      // dS^T buffer s was last read by the dQ^T MMA of block it - 2
+      if (it >= 2 && !(ok = warp_wait(&sm.pds_free[s], ((it >> 1) - 1) & 1, status, kBwdWaitPdsFree))) break;
 #pragma unroll
       for (int g = 0; g < 4; ++g)
-        *reinterpret_cast<uint4*>(sm.dst + swz(r, half * 4 + g)) =
+        *reinterpret_cast<uint4*>(sm.dst[s] + swz(r, half * 4 + g)) =
             make_uint4(dk[g * 4], dk[g * 4 + 1], dk[g * 4 + 2], dk[g * 4 + 3]);
       fence_proxy_async_smem();
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&sm.pds_ready);
+      if (lane == 0) TDSV_TRACE(6 + warp, it);  // events 8..15: pds_ready arrival of warps 2..9
       if (it >= 1) {
         if (!(ok = warp_wait(&sm.dq_full, (it - 1) & 1, status, kBwdWaitDq))) break;
         tc_fence_after();
@@ -759,7 +804,14 @@ std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const
 
 // Gradients of attn_fwd: (dq, dk, dv) in the layouts of q, k, v.
 std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
-                                 const at::Tensor& v, const at::Tensor& out, const at::Tensor& lse) {
+                                 const at::Tensor& v, const at::Tensor& out, const at::Tensor& lse,
+                                 const c10::optional<at::Tensor>& trace) {
+  long long* trace_ptr = nullptr;
+  if (trace.has_value() && trace->defined()) {
+    check_cuda_tensor(*trace, "attention trace");
+    TDSV_CHECK(trace->scalar_type() == at::kLong && trace->numel() >= 16 * 64, "attention trace: int64 [16, 64]");
+    trace_ptr = reinterpret_cast<long long*>(trace->data_ptr());
+  }
   check_operands(q, k, v);
   check_cuda_tensor(dout, "attention dout");
   check_cuda_tensor(out, "attention out");
@@ -799,7 +851,7 @@ std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, co
   dim3 grid(static_cast<unsigned>(heads), static_cast<unsigned>(seq / kTile), static_cast<unsigned>(batch));
   attn_bwd_kernel<<<grid, kBwdThreads, smem, stream()>>>(mq, mk, mv, mdo, mdk, mdv, dq_acc, lse2, dvec,
                                                          static_cast<int>(seq), heads, kv_heads, kLog2e * scale,
-                                                         status_word_ptr());
+                                                         status_word_ptr(), trace_ptr);
   TDSV_LAUNCH_CHECK();
 
   const int64_t nq8 = n_q / 8, nkv8 = n_kv / 8;

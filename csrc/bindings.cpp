@@ -121,7 +121,8 @@ at::Tensor index_scores(const at::Tensor& query, const at::Tensor& keys, const a
 std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                                  const c10::optional<at::Tensor>& trace);
 std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
-                                 const at::Tensor& v, const at::Tensor& out, const at::Tensor& lse);
+                                 const at::Tensor& v, const at::Tensor& out, const at::Tensor& lse,
+                                 const c10::optional<at::Tensor>& trace);
 }  // namespace tdsv
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -134,7 +135,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_dest_plan", &tdsv::ep_dest_plan, "per-token destination ranks, receive slots and counts");
   m.def("attn_fwd", &tdsv::attn_fwd, "causal GQA flash attention forward (tcgen05): (out, lse)", py::arg("q"),
         py::arg("k"), py::arg("v"), py::arg("trace") = py::none());
-  m.def("attn_bwd", &tdsv::attn_bwd, "causal GQA flash attention backward (tcgen05): (dq, dk, dv)");
+  m.def("attn_bwd", &tdsv::attn_bwd, "causal GQA flash attention backward (tcgen05): (dq, dk, dv)", py::arg("dout"),
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("lse"), py::arg("trace") = py::none());
   m.def("index_scores", &tdsv::index_scores, "DSV4 sparse-indexer scores (tcgen05, fused relu / head reduction)");
   m.def("fp4_dequant", &tdsv::fp4_dequant, "MXFP4 (E2M1 + E8M0 per 32) to bf16");
   m.def("rmsnorm_fwd", &tdsv::rmsnorm_fwd);

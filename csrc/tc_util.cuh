@@ -57,10 +57,34 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t base, int kk, uint32_t
   return make_smem_desc_sw128(base + kk * 2048, atom_bytes, 1024);
 }
 
+// Bounded wait with mbarrier.try_wait and a suspend-time hint: the thread sleeps in hardware until
+// the phase completes instead of polling and taking issue slots from the warps on its scheduler.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(1000000u)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_sleep_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
+  if (mbar_try_wait_sleep(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if (global_timer_ns() - start > kWaitLimitNs) break;
+  }
+  report_status(status, code);
+  return false;
+}
+
 // Bounded wait taken by a whole warp: every lane reaches the vote, so the warp leaves converged
 // (tcgen05.ld / st are warp-collective) and takes a timeout branch together.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int* status, int code) {
-  return __all_sync(0xffffffffu, mbar_wait(bar, parity, status, code));
+  return __all_sync(0xffffffffu, mbar_sleep_wait(bar, parity, status, code));
 }
 
 // 2^x by the special-function unit (PTX ex2.approx.ftz.f32; denormal results flush to zero and
@@ -70,6 +94,7 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+
 
 // Byte offset of 16-byte chunk `chunk` of row `row` in a 128-byte-swizzled atom.
 __device__ __forceinline__ uint32_t swz(int row, int chunk) {
