@@ -115,6 +115,19 @@ def cases():
             return torch.autograd.grad(ref_out, (qr, kr, vr), dref, retain_graph=True)
         return (lambda: C.attn_bwd(dout, q, k, v, out, lse)), sdpa_bwd, int(2.5 * fwd_flops), None
 
+    def index_scores(batch=1, seq=4096, heads=32, dim=128, ratio=4):
+        # DeepSeek-V4-Flash indexer shape: 32 heads x 128, one compressed key per `ratio` tokens;
+        # FLOPs of the dense score tile (queries x visible-key window x heads x dim)
+        keys_len = seq // ratio
+        q = torch.randn(batch, seq, heads, dim, device=dev, dtype=bf)
+        k = torch.randn(batch, keys_len, dim, device=dev, dtype=bf)
+        w = torch.randn(batch, seq, heads, device=dev) * heads ** -0.5
+        starts = torch.zeros(batch, seq, dtype=torch.int32, device=dev)
+        ends = ((torch.arange(seq, device=dev) + 1) // ratio).clamp_min(1).to(torch.int32).expand(batch, seq).contiguous()
+        width = keys_len
+        flops = 2 * batch * seq * width * heads * dim
+        return (lambda: C.index_scores(q, k, w, starts, ends, width, None)), None, flops, None
+
     return {
         "dense_lm_head": lambda: dense(4096, 151936, 2048),
         "dense_qkv": lambda: dense(4096, 5120, 2048),
@@ -127,6 +140,7 @@ def cases():
         "rmsnorm": rmsnorm,
         "attn_fwd": lambda: attention("fwd"),
         "attn_bwd": lambda: attention("bwd"),
+        "index_scores": index_scores,
     }
 
 

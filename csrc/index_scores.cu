@@ -12,7 +12,8 @@
 //
 //   warp 0     TMA producer: the Q block once, then key tiles through a three-stage ring
 //   warp 1     MMA issuer (M = 128 keys, N = 128 rows, K = head dim), TMEM double-buffered
-//   warps 2-5  epilogue: relu, head weights, head reduction, masked coalesced stores
+//   warps 2-9  epilogue, two per TMEM lane quarter (each owns half of the block's queries): relu,
+//              head weights, head reduction in registers, masked coalesced stores
 //
 // Reference: dsv41_train/models/dsv4/attention/sparse_indexer.py:17-78 (Triton, one program per
 // query and 64 keys) and its PyTorch restatement at lines 156-172.
@@ -48,10 +49,14 @@ struct IdxSmem {
   uint32_t tmem_base;
 };
 
-__global__ void __launch_bounds__(192, 1) index_scores_kernel(
+constexpr int kThreads = 320;  // TMA warp, MMA warp, 8 epilogue warps (two per TMEM lane quarter)
+
+template <int H>
+__global__ void __launch_bounds__(kThreads, 1) index_scores_kernel(
     const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk, const float* __restrict__ weights,
     const int* __restrict__ starts, const int* __restrict__ ends, const bool* __restrict__ candidates,
-    float* __restrict__ out, int seq, int key_len, int heads, int dim, int width, float scale, int* __restrict__ status) {
+    float* __restrict__ out, int seq, int key_len, int dim, int width, float scale, int* __restrict__ status) {
+  constexpr int heads = H;
   extern __shared__ uint8_t smem_raw[];
   IdxSmem& sm = *reinterpret_cast<IdxSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -97,7 +102,7 @@ __global__ void __launch_bounds__(192, 1) index_scores_kernel(
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&sm.acc_full[s], 1);
-      mbar_init(&sm.acc_free[s], 128);
+      mbar_init(&sm.acc_free[s], 256);
     }
     fence_barrier_init();
   }
@@ -142,40 +147,47 @@ __global__ void __launch_bounds__(192, 1) index_scores_kernel(
       }
     }
   } else {
-    const int quarter = warp & 3;
-    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
+    // thread <-> key (TMEM lane); `half` owns accumulator columns [64 half, 64 half + 64), i.e. the
+    // queries [64 half / H, (64 half + 64) / H) of the block (all heads of a query in one half)
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16) + half * 64;
     const int64_t out_row0 = qrow0 * width;
+    constexpr int G = H < 32 ? H : 32;  // heads of one query inside a 32-column chunk
     for (int t = 0; t < ntiles; ++t) {
       const int buf = t & 1;
       if (!warp_wait(&sm.acc_full[buf], (t >> 1) & 1, status, kWaitAcc)) break;
       tc_fence_after();
+      uint32_t v[2][32];
+      tmem_ld_32x32b_x32(lane_addr + buf * kRows, v[0]);
+      tmem_ld_32x32b_x32(lane_addr + buf * kRows + 32, v[1]);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&sm.acc_free[buf]);
       const int key = kmin + t * kRows + quarter * 32 + lane;
       float acc = 0.f;
-      for (int chunk = 0; chunk < kRows / 32; ++chunk) {
-        uint32_t v[32];
-        __syncwarp();  // the masked stores of the previous chunk may have split the warp
-        tmem_ld_32x32b_x32(lane_addr + buf * kRows + chunk * 32, v);
-        tmem_ld_wait();
-        if (chunk == kRows / 32 - 1) {
-          tc_fence_before();
-          mbar_arrive(&sm.acc_free[buf]);
-        }
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int n = chunk * 32 + i;
-          acc = fmaf(sm.w[n], fmaxf(__uint_as_float(v[i]), 0.f), acc);
-          if (((n + 1) & (heads - 1)) == 0) {  // last head of query n / heads
-            const int q = n / heads;
-            const int c = key - sm.start[q];
-            if (l0 + q < seq && c >= 0 && c < width) {
-              const int64_t o = out_row0 + static_cast<int64_t>(q) * width + c;
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int g0 = 0; g0 < 32; g0 += G) {
+          const int n0 = half * 64 + c * 32 + g0;  // first accumulator column of this head group
+          float s0 = 0.f, s1 = 0.f;
+#pragma unroll
+          for (int i = 0; i < G; i += 2) {
+            s0 = fmaf(sm.w[n0 + i], fmaxf(__uint_as_float(v[c][g0 + i]), 0.f), s0);
+            s1 = fmaf(sm.w[n0 + i + 1], fmaxf(__uint_as_float(v[c][g0 + i + 1]), 0.f), s1);
+          }
+          acc += s0 + s1;
+          if ((n0 + G) % H == 0) {  // last head group of query n0 / H
+            const int q = n0 / H;
+            const int col = key - sm.start[q];
+            if (l0 + q < seq && col >= 0 && col < width) {
+              const int64_t o = out_row0 + static_cast<int64_t>(q) * width + col;
               const bool valid = key < sm.end[q] && (candidates == nullptr || candidates[o]);
               out[o] = valid ? acc * scale : -INFINITY;
             }
             acc = 0.f;
           }
         }
-      }
     }
   }
   tc_fence_before();
@@ -219,7 +231,7 @@ at::Tensor index_scores(const at::Tensor& query, const at::Tensor& keys, const a
   const int64_t key_len = keys.size(1);
   TDSV_CHECK(keys.size(0) == batch && keys.size(2) == dim, "index scores: keys must share batch and head dim");
   TDSV_CHECK(dim == 64 || dim == 128, "index scores: head dim 64 or 128");
-  TDSV_CHECK(heads >= 1 && heads <= kRows && (heads & (heads - 1)) == 0, "index scores: heads a power of two <= 128");
+  TDSV_CHECK(heads >= 4 && heads <= 64 && (heads & (heads - 1)) == 0, "index scores: heads a power of two in [4, 64]");
   TDSV_CHECK(weights.scalar_type() == at::kFloat && weights.numel() == batch * seq * heads, "index weights [B, L, H] fp32");
   TDSV_CHECK(starts.scalar_type() == at::kInt && ends.scalar_type() == at::kInt && starts.numel() == batch * seq &&
                  ends.numel() == batch * seq,
@@ -246,17 +258,25 @@ at::Tensor index_scores(const at::Tensor& query, const at::Tensor& keys, const a
   const CUtensorMap mq = bf16_map(query, 2, qdims, qstr, qbox);
   const CUtensorMap mk = bf16_map(keys, 3, kdims, kstr, kbox);
   const size_t smem = sizeof(IdxSmem) + 1024;
-  static std::once_flag once;
-  std::call_once(once, [&] {
-    TDSV_CUDA_CHECK(cudaFuncSetAttribute(index_scores_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem)));
-  });
   const int qb = static_cast<int>(kRows / heads);
   dim3 grid(static_cast<unsigned>((seq + qb - 1) / qb), static_cast<unsigned>(batch));
-  index_scores_kernel<<<grid, 192, smem, stream()>>>(
-      mq, mk, weights.data_ptr<float>(), starts.data_ptr<int>(), ends.data_ptr<int>(), cand, out.data_ptr<float>(),
-      static_cast<int>(seq), static_cast<int>(key_len), static_cast<int>(heads), static_cast<int>(dim),
-      static_cast<int>(width), 1.f / sqrtf(static_cast<float>(dim)), status_word_ptr());
+  auto launch = [&](auto kernel) {
+    static std::once_flag once[7];
+    std::call_once(once[__builtin_ctz(static_cast<unsigned>(heads))], [&] {
+      TDSV_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    });
+    kernel<<<grid, kThreads, smem, stream()>>>(mq, mk, weights.data_ptr<float>(), starts.data_ptr<int>(),
+                                               ends.data_ptr<int>(), cand, out.data_ptr<float>(), static_cast<int>(seq),
+                                               static_cast<int>(key_len), static_cast<int>(dim), static_cast<int>(width),
+                                               1.f / sqrtf(static_cast<float>(dim)), status_word_ptr());
+  };
+  switch (heads) {
+    case 4: launch(index_scores_kernel<4>); break;
+    case 8: launch(index_scores_kernel<8>); break;
+    case 16: launch(index_scores_kernel<16>); break;
+    case 32: launch(index_scores_kernel<32>); break;
+    default: launch(index_scores_kernel<64>); break;
+  }
   TDSV_LAUNCH_CHECK();
   return out;
 }

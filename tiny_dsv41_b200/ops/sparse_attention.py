@@ -12,7 +12,7 @@ keys (``sparse_indexer.py:156-172``), -inf outside [start, end) or outside the c
 
 On CUDA, ``index_scores`` runs the tcgen05 kernel of ``csrc/index_scores.cu`` (keys as the M
 operand, the block's (query, head) rows as N, relu / head weights / head reduction in the TMEM
-epilogue; head dim 64 or 128, heads a power of two). ``sparse_attention`` is a gathered batched
+epilogue; head dim 64 or 128, heads a power of two from 4 to 64). ``sparse_attention`` is a gathered batched
 matmul (cuBLAS through PyTorch); its own kernel is not built yet. The PyTorch restatements below
 are the oracle on CPU.
 """
@@ -55,7 +55,7 @@ def sparse_attention(query, kv, window_indices, window_mask, compressed_kv, comp
 def _index_kernel_ok(query, keys, weights, width, candidates) -> bool:
     heads, dim = query.shape[2], query.shape[3]
     return (query.dtype == torch.bfloat16 and keys.dtype == torch.bfloat16 and dim in (64, 128)
-            and 1 <= heads <= 128 and heads & (heads - 1) == 0 and width > 0
+            and 4 <= heads <= 64 and heads & (heads - 1) == 0 and width > 0
             and (candidates is None or candidates.numel() == query.shape[0] * query.shape[1] * width))
 
 
