@@ -123,3 +123,24 @@ def test_local_grpo_run_and_resume(tmp_path):
                    str(tmp_path / "eval")])
     metrics = json.loads((tmp_path / "eval" / "eval-metrics.jsonl").read_text().splitlines()[-1])
     assert metrics["step"] == 3 and metrics["prompts"] == 4
+
+
+def test_qwen_head_example_runs_and_checkpoints(tmp_path):
+    """The shipped tiny Qwen3-MoE fixture and lm_head-only config train through the manager and
+    close it cleanly (its recovery snapshot carries the sampler RNG state)."""
+    import json
+    import subprocess
+    import sys
+
+    root = Path(__file__).resolve().parents[1]
+    config = json.loads((root / "examples/rl/qwen-head.json").read_text())
+    config.update(max_steps=2, output_dir=str(tmp_path / "out"))
+    cfg_path = tmp_path / "qwen-head.json"
+    cfg_path.write_text(json.dumps(config))
+    proc = subprocess.run([sys.executable, "-m", "tiny_dsv41_b200.rl.train", "--model-dir",
+                           str(root / "examples/tiny-qwen3"), "--data", str(root / "examples/rl/prompts.jsonl"),
+                           "--config", str(cfg_path), "--random-init"],
+                          cwd=root, capture_output=True, text=True, timeout=600)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    state = torch.load(tmp_path / "out" / "step-00000002.pt", weights_only=False)
+    assert state["step"] == 2 and state["rollout_rng_state"].dtype == torch.uint8

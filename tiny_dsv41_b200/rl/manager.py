@@ -26,6 +26,8 @@ import uuid
 from dataclasses import asdict
 from pathlib import Path
 
+import torch
+
 
 def _encode(packet: dict) -> dict:
     return {**packet, "group": asdict(packet["group"])}
@@ -130,7 +132,7 @@ def _serve(connection, settings: dict) -> None:
 
     def snapshot():
         return {"schema_version": 1, "next_group_id": next_group, "committed_highwater": committed,
-                "dropped_groups": dropped, "rng_state": sampler.rng_state(),
+                "dropped_groups": dropped, "rng_state": sampler.rng_state().numpy().tobytes(),
                 "pending_packets": [_encode(retained[k]["packet"]) for k in sorted(retained)],
                 "active_policy": dict(sampler.artifact), "policy_ack": dict(sampler.ack),
                 "queue_capacity": config.queue_capacity, "retained_capacity": bound, "admission_paused": True,
@@ -287,7 +289,7 @@ class RolloutManager:
             time.sleep(min(0.01, remaining))
 
     def pause(self):
-        return self._rpc("pause")
+        return _restore_rng_tensor(self._rpc("pause"))
 
     def commit(self, consumed_group_ids=(), dropped_group_ids=()):
         return self._rpc("commit", consumed=list(consumed_group_ids), dropped=list(dropped_group_ids))
@@ -324,7 +326,18 @@ class RolloutManager:
                 self.connection.close()
         if failure and not prior_failure:
             raise failure
+        if result is not None:
+            result = dict(result, recovery=_restore_rng_tensor(result.get("recovery")))
         return result
+
+
+def _restore_rng_tensor(snapshot):
+    """The child sends its generator state as bytes: a tensor would cross the pipe as a shared-memory
+    file descriptor that the child's exit (right after its ``close`` reply) can revoke before the
+    parent has fetched it. Callers and checkpoints get the usual uint8 tensor back."""
+    if snapshot and isinstance(snapshot.get("rng_state"), (bytes, bytearray)):
+        snapshot = dict(snapshot, rng_state=torch.frombuffer(bytearray(snapshot["rng_state"]), dtype=torch.uint8))
+    return snapshot
 
 
 __all__ = ["RolloutManager"]
