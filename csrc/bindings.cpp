@@ -113,6 +113,8 @@ void ep_combine_push(const at::Tensor& y, const at::Tensor& route, const c10::op
                      const at::Tensor& peer_flags, int64_t my_rank, int64_t epoch);
 at::Tensor ep_reduce_returned(const at::Tensor& ret, const at::Tensor& dest_mask, const at::Tensor& slot,
                               int64_t tokens);
+// fake_quant.cu
+at::Tensor cache_fake_quant(const at::Tensor& x, int64_t kind);
 // index_scores.cu
 at::Tensor index_scores(const at::Tensor& query, const at::Tensor& keys, const at::Tensor& weights,
                         const at::Tensor& starts, const at::Tensor& ends, int64_t width,
@@ -137,6 +139,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("k"), py::arg("v"), py::arg("trace") = py::none());
   m.def("attn_bwd", &tdsv::attn_bwd, "causal GQA flash attention backward (tcgen05): (dq, dk, dv)", py::arg("dout"),
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("lse"), py::arg("trace") = py::none());
+  m.def("cache_fake_quant", &tdsv::cache_fake_quant, "FP8 / FP4 block fake quantization (0 fp8, 1 fp4_index, 2 fp4_kv)");
   m.def("index_scores", &tdsv::index_scores, "DSV4 sparse-indexer scores (tcgen05, fused relu / head reduction)");
   m.def("fp4_dequant", &tdsv::fp4_dequant, "MXFP4 (E2M1 + E8M0 per 32) to bf16");
   m.def("rmsnorm_fwd", &tdsv::rmsnorm_fwd);

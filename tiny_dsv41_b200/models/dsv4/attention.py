@@ -18,6 +18,7 @@ import torch.nn.functional as F
 from torch import nn
 
 from ... import ops
+from ...ops.quant import quantize_activation
 from ...ops.sparse_attention import index_scores, sparse_attention
 from ...parallel.cp import ModelContext
 from ..common import Linear
@@ -211,6 +212,7 @@ class SparseIndexer(nn.Module):
         self.topk = config.index_topk
         self.topk_blocks = config.candidate_topk_blocks
         self.block_size = config.candidate_block_size
+        self.quantized_cache = config.cache_quantization == "hf"
         self.ratio = config.compress_ratios[layer_id]
         self.rotary = rotary
         self.q_proj = Linear(config.q_lora_rank, self.num_heads * self.head_dim, bias=False)
@@ -224,8 +226,10 @@ class SparseIndexer(nn.Module):
         if self.owns_keys:
             shadow.index_keys = None
             if latent is not None:
-                keys = self.k_norm(self.k_proj(latent))
-                shadow.index_keys = apply_rope(keys, group_positions, self.rotary.freqs(True)).unsqueeze(1)
+                keys = apply_rope(self.k_norm(self.k_proj(latent)), group_positions, self.rotary.freqs(True))
+                if self.quantized_cache:
+                    keys = quantize_activation(keys, "fp4_index")
+                shadow.index_keys = keys.unsqueeze(1)
         if shadow.index_keys is None:
             shadow.topk_indices = None
             if self.is_candidate_source:
@@ -244,6 +248,8 @@ class SparseIndexer(nn.Module):
         ends = torch.where(valid, ends, starts)
         query = self.q_proj(q_residual).view(batch, length, self.num_heads, self.head_dim)
         query = apply_rope(query, context.positions, self.rotary.freqs(True))
+        if self.quantized_cache:
+            query = quantize_activation(query, "fp4_index")
         head_weights = self.weight_proj(x).float() * self.num_heads ** -0.5
         width = int((seq_ends - starts).max().item())
         previous = shadow.candidates if self.uses_candidates else None
@@ -251,7 +257,8 @@ class SparseIndexer(nn.Module):
         if self.is_candidate_source:
             shadow.candidates = select_candidate_blocks(scores, ends - starts, self.topk_blocks, self.block_size,
                                                         stable=self.stable_topk)
-        values, idx = _select_topk(scores, min(self.topk, scores.shape[-1]), stable=self.stable_topk)
+        values, idx = _select_topk(scores, min(self.topk, scores.shape[-1]), stable=self.stable_topk,
+                                   sorted=self.quantized_cache)
         picked = starts.unsqueeze(-1) + idx
         shadow.topk_indices = torch.where(values > float("-inf"), picked, torch.full_like(picked, -1))
 
@@ -289,6 +296,8 @@ class CSA2Attention(nn.Module):
         query = self.q_b(q_residual).view(batch, length, self.num_heads, self.head_dim)
         query = apply_rope(query, context.positions, freqs).transpose(1, 2)
         kv = apply_rope(self.kv_norm(self.kv_proj(x)), context.positions, freqs).unsqueeze(1)
+        if self.config.cache_quantization == "hf":
+            kv = quantize_activation(kv, "fp8")
         kv = context.gather_attention(kv, dim=2)[:, 0]
         entries = topk = None
         if compressed:
@@ -304,7 +313,10 @@ class CSA2Attention(nn.Module):
                 with torch.no_grad():
                     self.indexer(x, q_residual, latent, group_positions, context, shadow)
             if latent is not None:
-                shadow.compressed_kv = apply_rope(latent, group_positions, self.rotary.freqs(True)).unsqueeze(1)
+                rotated = apply_rope(latent, group_positions, self.rotary.freqs(True))
+                if self.config.cache_quantization == "hf":
+                    rotated = quantize_activation(rotated, "fp4_kv")
+                shadow.compressed_kv = rotated.unsqueeze(1)
             if shadow.compressed_kv is not None and shadow.topk_indices is not None:
                 entries = shadow.compressed_kv[:, 0]
                 topk = shadow.topk_indices

@@ -85,9 +85,11 @@ def load_dsv41_backbone_window(folder, *, start_layer: int = 0, num_layers: int 
                                dtype=torch.bfloat16, context_parallel=None, token_dispatcher=None, engram_mesh=None,
                                sparse_engram_gradients: bool = False,
                                layer_loaded: Callable | None = None, engram_weights=None,
-                               engram_offload: bool = False, fp4_experts: bool = False) -> DeepSeekV41ForCausalLM:
+                               engram_offload: bool = False, fp4_experts: bool = False,
+                               cache_quantization: str | None = None) -> DeepSeekV41ForCausalLM:
     """``fp4_experts`` keeps the routed experts as frozen MXFP4 codes + E8M0 scales (uint8 buffers,
-    expanded per GEMM) instead of dequantising them to ``dtype`` at load."""
+    expanded per GEMM) instead of dequantising them to ``dtype`` at load. ``cache_quantization``
+    ("none" / "hf") overrides the checkpoint config's setting."""
     folder = Path(folder)
     if engram_offload and engram_weights is not None:
         raise ValueError("trainable CPU offload cannot reuse frozen shared Engram weights")
@@ -102,6 +104,8 @@ def load_dsv41_backbone_window(folder, *, start_layer: int = 0, num_layers: int 
         if start_layer not in config.kv_source_layer_ids:
             raise ValueError("a non-prefix layer window must start at a KV source layer")
         layer_ids = list(range(start_layer, stop))
+    if cache_quantization is not None:
+        config = DeepSeekV41Config.from_dict({**config.to_dict(), "cache_quantization": cache_quantization})
     with torch.device("meta"):
         model = DeepSeekV41ForCausalLM(config, context_parallel, token_dispatcher, engram_mesh, layer_ids,
                                        sparse_engram_gradients, engram_offload)

@@ -66,6 +66,9 @@ class DeepSeekV41Config:
     initializer_range: float
     rms_norm_eps: float
     router_aux_loss_coef: float = 0.001
+    # "hf": score with the values an FP8 / FP4 KV cache returns (window KV in FP8, compressed KV and
+    # indexer keys / queries in FP4), as the rollout engine sees them; gradients pass straight through
+    cache_quantization: str = "none"
     pad_token_id: int
     bos_token_id: int
     eos_token_id: int | list[int]
@@ -107,6 +110,8 @@ class DeepSeekV41Config:
                 raise ValueError(f"compressed layer {layer} has no preceding KV source")
         if self.candidate_source_layer_id >= 0 and self.candidate_source_layer_id not in self.index_source_layer_ids:
             raise ValueError("candidate_source_layer_id must be an index source")
+        if self.cache_quantization not in ("none", "hf"):
+            raise ValueError("cache_quantization must be none or hf")
 
     @classmethod
     def tiny(cls) -> "DeepSeekV41Config":

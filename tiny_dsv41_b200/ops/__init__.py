@@ -8,12 +8,13 @@ from .gemm import grouped_linear, linear, matmul_nt
 from .loss import linear_cross_entropy, token_log_probs
 from .moe import Routing, build_routing, combine, gather, swiglu
 from .norm import rms_norm
+from .quant import fake_quant, quantize_activation
 from . import rope
 from .rope import inv_freq, qk_norm_rope, rope_interleaved
 from .router import AuxGradient, route
 
 __all__ = [
     "AuxGradient", "Routing", "available", "build_routing", "causal_attention", "check_status", "combine",
-    "dequantize_fp4", "ext", "fp4_grouped_linear", "gather", "grouped_linear", "inv_freq", "linear", "linear_cross_entropy", "matmul_nt", "on_gpu",
-    "qk_norm_rope", "rms_norm", "rope_interleaved", "route", "swiglu", "token_log_probs",
+    "dequantize_fp4", "ext", "fake_quant", "fp4_grouped_linear", "gather", "grouped_linear", "inv_freq", "linear", "linear_cross_entropy", "matmul_nt", "on_gpu",
+    "qk_norm_rope", "quantize_activation", "rms_norm", "rope_interleaved", "route", "swiglu", "token_log_probs",
 ]

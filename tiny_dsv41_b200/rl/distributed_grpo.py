@@ -274,9 +274,12 @@ def load_learner(args, lora_config: DistributedLoRAConfig, device):
 
             dispatcher = AllToAllTokenDispatcher(meshes.ep)
     dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
+    # score with the values the rollout service's FP8 / FP4 KV cache returns (reference
+    # dsv41_train/rl/native_lora.py:208 loads its scoring model with cache_quantization="hf")
     model = load_dsv41_backbone_prefix(args.model_dir, num_layers=cfg.num_hidden_layers, device=device, dtype=dtype,
                                        context_parallel=ContextParallel(), token_dispatcher=dispatcher,
-                                       engram_mesh=meshes.engram if meshes is not None else None)
+                                       engram_mesh=meshes.engram if meshes is not None else None,
+                                       cache_quantization=args.cache_quantization)
     for p in model.parameters():
         p.requires_grad_(False)
     for layer in lora_config.selected_layers(cfg.num_hidden_layers):
@@ -453,6 +456,8 @@ def parse_args(argv=None):
     p.add_argument("--lora-rank", type=int, choices=SUPPORTED_LORA_RANKS, default=8)
     p.add_argument("--lora-alpha", type=float, default=8.0)
     p.add_argument("--lora-layers", type=parse_lora_layers, default=None)
+    p.add_argument("--cache-quantization", choices=("hf", "none"), default="hf",
+                   help="hf: score under the rollout engine's FP8 window-KV / FP4 compressed-KV and indexer cache")
     p.add_argument("--seed", type=int, default=42)
     p.add_argument("--max-prompt-tokens", type=int, default=256)
     p.add_argument("--max-new-tokens", type=int, default=256)
