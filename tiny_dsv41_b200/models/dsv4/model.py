@@ -35,6 +35,7 @@ from ...parallel import replay
 from ...parallel.cp import ContextParallel, ModelContext
 from ...parallel.dispatch import TokenDispatcher
 from ...parallel.engram_offload import CPUEmbeddingLookup
+from ...utils.trace import nvtx_range
 from ..common import Linear, LMHead
 from .attention import AttentionSinks, CSA2Attention, GroupedLinear, RMSNorm, RotaryEmbedding, ShadowIndexers
 from .config import DeepSeekV41Config
@@ -304,13 +305,15 @@ class DecoderLayer(nn.Module):
         if self.engram is not None:
             streams = self.engram(streams, engram_rows, context.token_mask)
         residual = streams
-        collapsed, next_pre, post, comb = self.attention_hc(streams, pre_mix)
-        value = self.attention(self.input_norm(collapsed), context, shadow)
-        streams = self.attention_hc.finish(value, residual, post, comb)
+        with nvtx_range("attention"):
+            collapsed, next_pre, post, comb = self.attention_hc(streams, pre_mix)
+            value = self.attention(self.input_norm(collapsed), context, shadow)
+            streams = self.attention_hc.finish(value, residual, post, comb)
         residual = streams
-        collapsed, final_pre, post, comb = self.moe_hc(streams, next_pre)
-        value, logits = self.moe(self.post_attention_norm(collapsed))
-        streams = self.moe_hc.finish(value, residual, post, comb)
+        with nvtx_range("moe"):
+            collapsed, final_pre, post, comb = self.moe_hc(streams, next_pre)
+            value, logits = self.moe(self.post_attention_norm(collapsed))
+            streams = self.moe_hc.finish(value, residual, post, comb)
         return streams, final_pre, logits
 
 

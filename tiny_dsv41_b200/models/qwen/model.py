@@ -26,6 +26,7 @@ from ...ops.router import AuxGradient
 from ...parallel import replay
 from ...parallel.cp import ContextParallel
 from ...parallel.dispatch import TokenDispatcher
+from ...utils.trace import nvtx_range
 from ..common import Linear, LMHead, fusable
 from .config import Qwen3MoeConfig
 
@@ -174,8 +175,10 @@ class Qwen3MoeDecoderLayer(nn.Module):
         self.post_attention_layernorm = Qwen3MoeRMSNorm(config.hidden_size, config.rms_norm_eps)
 
     def forward(self, hidden, position_ids, attention_mask=None, cache=None):
-        hidden = hidden + self.self_attn(self.input_layernorm(hidden), position_ids, attention_mask, cache)
-        out = self.mlp(self.post_attention_layernorm(hidden))
+        with nvtx_range("attention"):
+            hidden = hidden + self.self_attn(self.input_layernorm(hidden), position_ids, attention_mask, cache)
+        with nvtx_range("moe"):
+            out = self.mlp(self.post_attention_layernorm(hidden))
         logits = None
         if isinstance(out, tuple):
             out, logits = out

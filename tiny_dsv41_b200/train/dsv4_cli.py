@@ -24,6 +24,7 @@ from ..parallel.cp import ContextParallel, pack_sequences
 from ..parallel.dispatch import TokenDispatcher
 from ..parallel.fsdp import apply_fsdp, expert_parameters, scale_expert_grads
 from ..runtime import distributed_mean, initialize_runtime, local_tensor
+from ..utils.trace import trace_point
 
 IN_BACKWARD_SCALE = 2.0 ** -16
 
@@ -105,6 +106,7 @@ def train(args, runtime) -> dict:
         model.gradient_checkpointing_enable()
     model.train()
     loaded = time.perf_counter()
+    trace_point("loaded", seconds=loaded - started)
     experts = sum(p.numel() for p in expert_parameters(model))
     tables = list(model.model.engram_tables.values())
     local_engram = sum(t.weight.numel() for t in tables)
@@ -114,6 +116,7 @@ def train(args, runtime) -> dict:
     if meshes is not None:
         apply_fsdp(model, meshes, param_dtype=dtype)
     sharded = time.perf_counter()
+    trace_point("sharded", seconds=sharded - loaded)
     tracked = model.model.layers[0].attention_hc.fn
     before = local_tensor(tracked).detach().float().clone()
     scale = IN_BACKWARD_SCALE if args.optimizer_in_backward else 1.0
@@ -134,6 +137,7 @@ def train(args, runtime) -> dict:
     generator.manual_seed(args.seed + runtime.rank // args.cp_size)
     loss_v = aux_v = 0.0
     for step in range(1, args.steps + 1):
+        trace_point("step_begin", step=step)
         ids = torch.randint(3, model.config.vocab_size, (args.batch_size, args.seq_len), device=runtime.device,
                             generator=generator)
         ids[:, 0] = model.config.bos_token_id
@@ -159,6 +163,7 @@ def train(args, runtime) -> dict:
             optimizer.step()
         loss_v = distributed_mean(out.loss, runtime)
         aux_v = distributed_mean(out.aux_loss, runtime)
+        trace_point("step_end", step=step, loss=loss_v)
         if runtime.is_main:
             print(json.dumps({"step": step, "loss": loss_v, "aux_loss": aux_v}), flush=True)
     delta = (local_tensor(tracked).detach().float() - before).abs().max()

@@ -22,6 +22,7 @@ from ..parallel.cp import ContextParallel
 from ..parallel.dispatch import TokenDispatcher
 from ..parallel.fsdp import apply_fsdp, clip_grad_norm_, expert_parameters, scale_expert_grads
 from ..runtime import distributed_mean, initialize_runtime, local_tensor
+from ..utils.trace import trace_point
 
 
 def parse_args(argv=None):
@@ -99,6 +100,7 @@ def train(args, runtime) -> dict:
     before = local_tensor(tracked).detach().float().clone()
     loss_v = aux_v = norm_v = 0.0
     for step in range(1, args.steps + 1):
+        trace_point("step_begin", step=step)
         ids = torch.randint(0, model.config.vocab_size, (args.batch_size, args.seq_len), device=runtime.device,
                             generator=generator)
         ids[:, 0] = model.config.bos_token_id
@@ -114,6 +116,7 @@ def train(args, runtime) -> dict:
         if isinstance(out.aux_loss, torch.Tensor):
             aux_v = distributed_mean(out.aux_loss, runtime)
         norm_v = float(norm)
+        trace_point("step_end", step=step, loss=loss_v, grad_norm=norm_v)
         if runtime.is_main:
             print(json.dumps({"step": step, "loss": loss_v, "aux_loss": aux_v, "grad_norm": norm_v}), flush=True)
     delta = (local_tensor(tracked).detach().float() - before).abs().max()

@@ -33,6 +33,7 @@ from ..parallel.fsdp import scale_expert_grads
 from ..rl.checkpoint import run_identity
 from ..rl.tokenizer import ModelTokenizer
 from ..runtime import initialize_runtime, local_tensor
+from ..utils.trace import trace_point
 from .sft_checkpoint import load_checkpoint, save_checkpoint
 from .sft_data import collate_examples, load_jsonl
 
@@ -327,12 +328,14 @@ def train(args, runtime) -> dict:
     loop_started = time.perf_counter()
     for step in range(initial + 1, args.steps + 1):
         batches, next_cursor = make_batches(examples, cursor, count=args.gradient_accumulation_steps, **options)
+        trace_point("step_begin", step=step, data_position=cursor)
         t0 = time.perf_counter()
         metrics = train_update(model, optimizer, batches, family=args.family, runtime=runtime, cp_size=args.cp_size,
                                ep_size=args.ep_size)
         if runtime.device.type == "cuda":
             torch.cuda.synchronize(runtime.device)
         metrics["seconds"] = time.perf_counter() - t0
+        trace_point("step_end", step=step, seconds=metrics["seconds"])
         cursor = next_cursor
         emit({"event": "train", "step": step, "data_position": cursor, **metrics})
         if not args.no_save and args.save_every and step % args.save_every == 0:
