@@ -39,6 +39,7 @@ enum StatusCode : int {
   kTimeoutAccumFree = 4, // MMA warp waited too long for the epilogue to drain TMEM
   kTimeoutPeer = 5,      // a peer rank never raised its flag
   kBadShape = 6,
+  kOutOfBounds = 7,      // a computed index fell outside its buffer (TDSV_BOUNDS_CHECK builds only)
 };
 
 
@@ -48,6 +49,15 @@ void check_status(const char* what);  // host: read, reset and raise if non-zero
 __device__ __forceinline__ void report_status(int* status, int code) {
   if (status != nullptr) atomicCAS(status, 0, code);
 }
+
+// Compile-time debug mode (build with TDSV_BOUNDS_CHECK=1): index-driven kernels test each computed
+// index with TDSV_IN_BOUNDS; an index out of range records kOutOfBounds in the status word and the
+// access is skipped. In normal builds the test is the constant `true` and compiles away.
+#ifdef TDSV_BOUNDS_CHECK
+#define TDSV_IN_BOUNDS(cond, status) ((cond) || (::tdsv::report_status((status), ::tdsv::kOutOfBounds), false))
+#else
+#define TDSV_IN_BOUNDS(cond, status) true
+#endif
 
 // ---------------------------------------------------------------------------------------------
 // Scalar helpers

@@ -66,7 +66,7 @@ __global__ void push_rows_kernel(const __nv_bfloat16* __restrict__ x, const uint
                                  const float* __restrict__ weights, int64_t tokens, int h, int ep, int my_rank,
                                  int64_t t_cap, int k, int e_local, unsigned int* __restrict__ done_counter,
                                  const int64_t* __restrict__ peer_flags, const int64_t* __restrict__ peer_counts,
-                                 const int32_t* __restrict__ counts, uint32_t epoch) {
+                                 const int32_t* __restrict__ counts, uint32_t epoch, int* status) {
   const int lane = threadIdx.x & 31;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t < tokens) {
@@ -74,7 +74,9 @@ __global__ void push_rows_kernel(const __nv_bfloat16* __restrict__ x, const uint
     const int vecs = h / 8;
     for (int d = 0; d < ep; ++d) {
       if (!dest_mask[t * ep + d]) continue;
-      const int64_t row = static_cast<int64_t>(my_rank) * t_cap + slot[t * ep + d];
+      const int sl = slot[t * ep + d];
+      if (!TDSV_IN_BOUNDS(sl >= 0 && sl < t_cap, status)) continue;  // a peer-memory write: never out of range
+      const int64_t row = static_cast<int64_t>(my_rank) * t_cap + sl;
       uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(peer_recv[d]) + row * h);
       for (int v = lane; v < vecs; v += 32) dst[v] = src[v];
       if (peer_meta != nullptr && lane < k) {
@@ -111,7 +113,8 @@ __global__ void combine_push_kernel(const __nv_bfloat16* __restrict__ y, const i
                                     const int64_t* __restrict__ peer_ret, const float* __restrict__ row_extra,
                                     const int64_t* __restrict__ peer_retw, int64_t t_cap, int h, int ep, int my_rank,
                                     int k, unsigned int* __restrict__ done_counter,
-                                    const int64_t* __restrict__ peer_flags, uint32_t epoch) {
+                                    const int64_t* __restrict__ peer_flags, uint32_t epoch, int64_t y_rows,
+                                    int* status) {
   const int lane = threadIdx.x & 31;
   const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int s = static_cast<int>(r / t_cap);
@@ -122,7 +125,7 @@ __global__ void combine_push_kernel(const __nv_bfloat16* __restrict__ y, const i
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       for (int j = 0; j < k; ++j) {
         const int row = route[r * k + j];
-        if (row < 0) continue;
+        if (row < 0 || !TDSV_IN_BOUNDS(row < y_rows, status)) continue;
         const float w = weights != nullptr ? weights[r * k + j] : 1.f;
         float v[8];
         load_bf16x8(y + static_cast<int64_t>(row) * h + c, v);
@@ -152,7 +155,7 @@ __global__ void combine_push_kernel(const __nv_bfloat16* __restrict__ y, const i
 // out[t] = sum over destination ranks d (ascending) with dest_mask[t,d] of ret[d][slot[t,d]].
 __global__ void reduce_returned_kernel(const __nv_bfloat16* __restrict__ ret, const uint8_t* __restrict__ dest_mask,
                                        const int32_t* __restrict__ slot, __nv_bfloat16* __restrict__ out,
-                                       int64_t tokens, int64_t t_cap, int h, int ep) {
+                                       int64_t tokens, int64_t t_cap, int h, int ep, int* status) {
   const int lane = threadIdx.x & 31;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t >= tokens) return;
@@ -160,8 +163,10 @@ __global__ void reduce_returned_kernel(const __nv_bfloat16* __restrict__ ret, co
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int d = 0; d < ep; ++d) {
       if (!dest_mask[t * ep + d]) continue;
+      const int sl = slot[t * ep + d];
+      if (!TDSV_IN_BOUNDS(sl >= 0 && sl < t_cap, status)) continue;
       float v[8];
-      load_bf16x8(ret + (static_cast<int64_t>(d) * t_cap + slot[t * ep + d]) * h + c, v);
+      load_bf16x8(ret + (static_cast<int64_t>(d) * t_cap + sl) * h + c, v);
 #pragma unroll
       for (int q = 0; q < 8; ++q) acc[q] += v[q];
     }
@@ -234,7 +239,7 @@ void ep_push_rows(const at::Tensor& x, const at::Tensor& dest_mask, const at::Te
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), dest_mask.data_ptr<uint8_t>(), slot.data_ptr<int32_t>(),
       peer_recv.data_ptr<int64_t>(), meta, idp, wp, tokens, h, ep, static_cast<int>(my_rank), t_cap, k,
       static_cast<int>(e_local), reinterpret_cast<unsigned int*>(done_counter.data_ptr()),
-      peer_flags.data_ptr<int64_t>(), pc, cnt, static_cast<uint32_t>(epoch));
+      peer_flags.data_ptr<int64_t>(), pc, cnt, static_cast<uint32_t>(epoch), status_word_ptr());
   TDSV_LAUNCH_CHECK();
 }
 
@@ -265,7 +270,7 @@ void ep_combine_push(const at::Tensor& y, const at::Tensor& route, const c10::op
       reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), route.data_ptr<int32_t>(), wp, counts.data_ptr<int32_t>(),
       peer_ret.data_ptr<int64_t>(), extra, retw, t_cap, h, ep, static_cast<int>(my_rank), k,
       reinterpret_cast<unsigned int*>(done_counter.data_ptr()), peer_flags.data_ptr<int64_t>(),
-      static_cast<uint32_t>(epoch));
+      static_cast<uint32_t>(epoch), y.size(0), status_word_ptr());
   TDSV_LAUNCH_CHECK();
 }
 
@@ -280,7 +285,7 @@ at::Tensor ep_reduce_returned(const at::Tensor& ret, const at::Tensor& dest_mask
   c10::cuda::CUDAGuard guard(ret.device());
   reduce_returned_kernel<<<(tokens + kWarpsPerBlock - 1) / kWarpsPerBlock, kWarpsPerBlock * 32, 0, stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(ret.data_ptr()), dest_mask.data_ptr<uint8_t>(), slot.data_ptr<int32_t>(),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), tokens, t_cap, h, ep);
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), tokens, t_cap, h, ep, status_word_ptr());
   TDSV_LAUNCH_CHECK();
   return out;
 }

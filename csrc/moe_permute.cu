@@ -18,7 +18,7 @@ namespace {
 
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, const int32_t* __restrict__ src,
                                    __nv_bfloat16* __restrict__ out, int64_t rows, int h,
-                                   const int32_t* __restrict__ row_limit) {
+                                   const int32_t* __restrict__ row_limit, int64_t src_rows, int* status) {
   // one warp per row, 16B vectors, grid-stride over the live rows
   const int lane = threadIdx.x & 31;
   const int64_t live = row_limit != nullptr ? min(rows, static_cast<int64_t>(*row_limit)) : rows;
@@ -28,7 +28,8 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, const in
 #pragma unroll
   for (int i = 0; i < 4; ++i) z.v[i] = __floats2bfloat162_rn(0.f, 0.f);
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < live; r += warps) {
-    const int s = src[r];
+    int s = src[r];
+    if (s >= 0 && !TDSV_IN_BOUNDS(s < src_rows, status)) s = -1;
     bf16x8* dst = reinterpret_cast<bf16x8*>(out + r * h);
     if (s < 0) {
       for (int v = lane; v < vecs; v += 32) dst[v] = z;
@@ -42,7 +43,7 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ x, const in
 // One warp per token (grid-stride); each lane owns 8 columns per pass.
 __global__ void combine_rows_kernel(const __nv_bfloat16* __restrict__ rows, const int32_t* __restrict__ idx,
                                     const float* __restrict__ w, __nv_bfloat16* __restrict__ out, int64_t tokens,
-                                    int k, int h) {
+                                    int k, int h, int64_t row_cap, int* status) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < tokens;
@@ -51,7 +52,7 @@ __global__ void combine_rows_kernel(const __nv_bfloat16* __restrict__ rows, cons
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int s = 0; s < k; ++s) {
       const int r = idx[t * k + s];
-      if (r < 0) continue;
+      if (r < 0 || !TDSV_IN_BOUNDS(r < row_cap, status)) continue;
       const float ws = w != nullptr ? w[t * k + s] : 1.f;
       float v[8];
       load_bf16x8(rows + static_cast<int64_t>(r) * h + c, v);
@@ -67,13 +68,14 @@ __global__ void combine_rows_kernel(const __nv_bfloat16* __restrict__ rows, cons
 __global__ void combine_rows_bwd_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ rows,
                                         const int32_t* __restrict__ idx, const float* __restrict__ w,
                                         __nv_bfloat16* __restrict__ drows, float* __restrict__ dw, int64_t tokens,
-                                        int k, int h) {
+                                        int k, int h, int64_t row_cap, int* status) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); t < tokens;
        t += warps)
   for (int s = 0; s < k; ++s) {
-    const int r = idx[t * k + s];
+    int r = idx[t * k + s];
+    if (r >= 0 && !TDSV_IN_BOUNDS(r < row_cap, status)) r = -1;
     float dot = 0.f;
     if (r >= 0) {
       const float ws = w != nullptr ? w[t * k + s] : 1.f;
@@ -138,7 +140,7 @@ at::Tensor moe_gather(const at::Tensor& x, const at::Tensor& src, const c10::opt
   c10::cuda::CUDAGuard guard(x.device());
   gather_rows_kernel<<<warp_grid(rows), 256, 0, stream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), src.data_ptr<int32_t>(),
-      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, h, limit_ptr(row_limit));
+      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, h, limit_ptr(row_limit), x.size(0), status_word_ptr());
   TDSV_LAUNCH_CHECK();
   return out;
 }
@@ -162,7 +164,8 @@ at::Tensor moe_combine(const at::Tensor& rows, const at::Tensor& idx, const c10:
   c10::cuda::CUDAGuard guard(rows.device());
   combine_rows_kernel<<<warp_grid(tokens), 256, 0, stream()>>>(reinterpret_cast<const __nv_bfloat16*>(rows.data_ptr()),
                                                         idx.data_ptr<int32_t>(), wp,
-                                                        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), tokens, k, h);
+                                                        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), tokens, k, h,
+                                                        rows.size(0), status_word_ptr());
   TDSV_LAUNCH_CHECK();
   return out;
 }
@@ -184,7 +187,7 @@ std::vector<at::Tensor> moe_combine_bwd(const at::Tensor& dout, const at::Tensor
     combine_rows_bwd_kernel<<<warp_grid(tokens), 256, 0, stream()>>>(
         reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(rows.data_ptr()),
         idx.data_ptr<int32_t>(), wp, reinterpret_cast<__nv_bfloat16*>(drows.data_ptr()),
-        need_dw ? dw.data_ptr<float>() : nullptr, tokens, k, h);
+        need_dw ? dw.data_ptr<float>() : nullptr, tokens, k, h, rows.size(0), status_word_ptr());
     TDSV_LAUNCH_CHECK();
   }
   return {drows, dw};

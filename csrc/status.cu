@@ -34,7 +34,8 @@ void check_status(const char* what) {
     TDSV_CUDA_CHECK(cudaStreamSynchronize(s));
     TORCH_CHECK(false, what, ": device pipeline reported status ", host,
                 " (1/2 = TMA stage wait timed out, 3/4 = accumulator wait timed out, 5 = peer flag "
-                "timed out, 6 = bad shape)");
+                "timed out, 6 = bad shape, 7 = index out of bounds (bounds-check build), 3xx / 4xx = "
+                "attention / indexer pipeline wait timed out)");
   }
 }
 

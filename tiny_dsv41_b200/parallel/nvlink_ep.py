@@ -16,16 +16,20 @@ tcgen05 grouped GEMMs.
 
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
 from .. import ops
 from ..ops import moe as moe_ops
+from ..utils.trace import nvtx_range
 from . import replay
 from .dispatch import DispatchBatch, TokenDispatcher
 
 # rows of the flag buffer
 _RECV_READY, _RECV_FREE, _RET_READY, _RET_FREE, _COUNTS = range(5)
+_CANARY = 0x5A5A  # int16 pattern of the debug guard rows
 
 
 class _Workspace:
@@ -36,15 +40,25 @@ class _Workspace:
 
         self.ep, self.rank, self.t_cap, self.hidden, self.k = ep, rank, t_cap, hidden, k
         self.device = device
-        self.recv = symm.empty(ep, t_cap, hidden, dtype=torch.bfloat16, device=device)
-        self.ret = symm.empty(ep, t_cap, hidden, dtype=torch.bfloat16, device=device)
+        # debug mode TDSV_EP_CANARY=1: one guard row after each row slab, filled with a pattern that
+        # check_canaries() verifies after every exchange (an out-of-range peer write lands there)
+        self.canary = os.environ.get("TDSV_EP_CANARY", "") not in ("", "0")
+        guard = 1 if self.canary else 0
+        recv = symm.empty(ep * t_cap + guard, hidden, dtype=torch.bfloat16, device=device)
+        ret = symm.empty(ep * t_cap + guard, hidden, dtype=torch.bfloat16, device=device)
+        self.recv = recv[:ep * t_cap].view(ep, t_cap, hidden)
+        self.ret = ret[:ep * t_cap].view(ep, t_cap, hidden)
+        self._guards = {"recv": recv[ep * t_cap:].view(torch.int16), "ret": ret[ep * t_cap:].view(torch.int16)}
+        for g in self._guards.values():
+            g.fill_(_CANARY)
+        self._slabs = {"recv": recv, "ret": ret}
         self.meta = symm.empty(ep, t_cap, 2 * k, dtype=torch.int32, device=device)
         self.retw = symm.empty(ep, t_cap, k, dtype=torch.float32, device=device)
         self.flags = symm.empty(5, ep, dtype=torch.int32, device=device)
         self.flags.zero_()
         handles = {}
         for name in ("recv", "ret", "meta", "retw", "flags"):
-            handles[name] = symm.rendezvous(getattr(self, name), group)
+            handles[name] = symm.rendezvous(self._slabs.get(name, getattr(self, name)), group)
         torch.cuda.synchronize(device)
         dist.barrier(group=group)
 
@@ -64,6 +78,15 @@ class _Workspace:
 
     def flag_row(self, row: int) -> torch.Tensor:
         return self.flags[row]
+
+    def check_canaries(self, where: str) -> None:
+        """Debug mode only (synchronises): raise if a guard row after a slab was overwritten."""
+        if not self.canary:
+            return
+        for name, guard in self._guards.items():
+            if not bool((guard == _CANARY).all()):
+                raise RuntimeError(f"NVLink EP: the guard row after the {name} slab was overwritten ({where}); "
+                                   "a peer wrote outside its slab")
 
 
 class _Exchange:
@@ -98,6 +121,7 @@ class _Exchange:
                        ws.peer_flags[_RECV_READY], ws.peer_flags[_COUNTS] if with_meta else None,
                        self.counts if with_meta else None, ws.rank, ws.recv_epoch)
         C.ep_wait(ws.flag_row(_RECV_READY), ws.recv_epoch)
+        ws.check_canaries("dispatch")
 
     def release_recv(self) -> None:
         ws = self.ws
@@ -113,6 +137,7 @@ class _Exchange:
                           ws.peer_retw if extra is not None else None, ws.t_cap, ws.done[1:2],
                           ws.peer_flags[_RET_READY], ws.rank, ws.ret_epoch)
         C.ep_wait(ws.flag_row(_RET_READY), ws.ret_epoch)
+        ws.check_canaries("combine")
 
     def release_ret(self) -> None:
         ws = self.ws
@@ -266,16 +291,17 @@ class NVLinkTokenDispatcher(TokenDispatcher):
         if not x.is_cuda:
             raise RuntimeError("the NVLink dispatcher needs CUDA tensors")
         handle, mode = replay.current()
-        if mode == "replay":
-            ex = handle.next()
-            rows, local_w = _ReplayDispatch.apply(x, weights, ids, ex)
-        else:
-            ws = self._workspace(x.shape[0], x.shape[1], ids.shape[1], x.device)
-            ex = _Exchange(ws, x.shape[0], self.num_experts // self.size)
-            ex.recording = mode == "record"
-            rows, local_w = _Dispatch.apply(x, weights, ids, ex)
-            if ex.recording:
-                handle.record(ex)
+        with nvtx_range("ep.dispatch"):
+            if mode == "replay":
+                ex = handle.next()
+                rows, local_w = _ReplayDispatch.apply(x, weights, ids, ex)
+            else:
+                ws = self._workspace(x.shape[0], x.shape[1], ids.shape[1], x.device)
+                ex = _Exchange(ws, x.shape[0], self.num_experts // self.size)
+                ex.recording = mode == "record"
+                rows, local_w = _Dispatch.apply(x, weights, ids, ex)
+                if ex.recording:
+                    handle.record(ex)
         ex.replaying = mode == "replay"
         routing = ex.routing
         return DispatchBatch(rows, routing.offsets, routing.rows, None,
@@ -290,7 +316,8 @@ class NVLinkTokenDispatcher(TokenDispatcher):
         local_w = batch.state["local_w"] if weighted else None
         if ex.replaying:
             return _ReplayCombine.apply(y, local_w, ex)
-        out = _Combine.apply(y, local_w, ex)
+        with nvtx_range("ep.combine"):
+            out = _Combine.apply(y, local_w, ex)
         if ex.recording:
             ex.cached_out = out.detach()
         return out
