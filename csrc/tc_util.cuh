@@ -38,7 +38,7 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
-// Plain bulk copy global -> shared (no multicast), completion on an mbarrier. 16-byte aligned, size % 16 == 0.
+// Plain bulk copy global -> this CTA's shared memory, completion on an mbarrier. 16-byte aligned, size % 16 == 0.
 __device__ __forceinline__ void bulk_load_1d(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    smem_u32(dst)),
