@@ -122,6 +122,10 @@ def test_dsv4_full_sft_engram_rows_resume(dsv4_dir, tmp_path):
     a, sa = _losses(tmp_path / "a")
     b, sb = _losses(tmp_path / "b")
     assert b[-2:] == pytest.approx(a[-2:], rel=1e-5)
+    steps = [json.loads(line) for line in (tmp_path / "a" / "metrics.jsonl").read_text().splitlines()]
+    step = next(r for r in steps if r["event"] == "train")
+    # offloaded Engram rows are looked up on the CPU path (no GPU row cache): the counters exist
+    assert {"seconds", "engram_cache_hits", "engram_cache_misses", "engram_cache_transferred_rows"} <= set(step)
     assert sb["eval_loss_after"] == pytest.approx(sa["eval_loss_after"], rel=1e-5)
 
 

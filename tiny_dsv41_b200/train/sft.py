@@ -198,6 +198,28 @@ def make_batches(examples, cursor: int, *, batch_size: int, count: int, runtime,
     return batches, cursor + count * data_size * batch_size
 
 
+def _step_resources(model, runtime, seconds: float) -> dict:
+    """Step seconds and peak device memory (max over ranks) and the Engram row-cache counters (sum
+    over ranks) of the offloaded tables; the reference's SFT step record (``train_sft.py:347-436``)."""
+    peak = [seconds, 0.0, 0.0]
+    if runtime.device.type == "cuda":
+        peak[1] = torch.cuda.max_memory_allocated(runtime.device) / 2 ** 30
+        peak[2] = torch.cuda.max_memory_reserved(runtime.device) / 2 ** 30
+    peak_t = _reduce(torch.tensor(peak, device=runtime.device, dtype=torch.float64), runtime,
+                     dist.ReduceOp.MAX if dist.is_initialized() else None)
+    out = {"seconds": peak_t[0].item()}
+    if runtime.device.type == "cuda":
+        out.update(peak_allocated_gib=round(peak_t[1].item(), 3), peak_reserved_gib=round(peak_t[2].item(), 3))
+    lookups = [m._cpu_lookup for m in model.modules() if getattr(m, "_cpu_lookup", None) is not None]
+    if lookups:
+        keys = ("hits", "misses", "transferred_rows")
+        counts = torch.tensor([sum(lk.cache_metrics[k] for lk in lookups) for k in keys], device=runtime.device,
+                              dtype=torch.float64)
+        counts = _reduce(counts, runtime)
+        out.update({f"engram_cache_{k}": int(v) for k, v in zip(keys, counts.tolist())})
+    return out
+
+
 def _reduce(value, runtime, op=None):
     if dist.is_initialized():
         dist.all_reduce(value, op=op or dist.ReduceOp.SUM)
@@ -334,7 +356,7 @@ def train(args, runtime) -> dict:
                                ep_size=args.ep_size)
         if runtime.device.type == "cuda":
             torch.cuda.synchronize(runtime.device)
-        metrics["seconds"] = time.perf_counter() - t0
+        metrics.update(_step_resources(model, runtime, time.perf_counter() - t0))
         trace_point("step_end", step=step, seconds=metrics["seconds"])
         cursor = next_cursor
         emit({"event": "train", "step": step, "data_position": cursor, **metrics})
