@@ -255,6 +255,11 @@ def run_training(*, model_dir, data_path, config: RLConfig, random_init=False, r
                         packet = manager.get(timeout=0.2)
                     except queue.Empty:
                         continue
+                    if packet.get("exclusion") is not None:  # a provider that rejected the group
+                        dropped += 1
+                        manager.commit(dropped_group_ids=[packet["group_id"]])
+                        append_jsonl(output_dir / "excluded-groups.jsonl", [packet["exclusion"]])
+                        continue
                     group = packet["group"]
                     lag = policy_lag(step, group.policy_version, config.max_policy_lag)
                     if lag is None:
