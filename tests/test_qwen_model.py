@@ -85,3 +85,21 @@ def test_kv_cache_sampling_matches_full_forward():
         assert a.response_ids == b.response_ids
         assert a.behavior_log_probs == pytest.approx(b.behavior_log_probs, abs=1e-5)
     assert policy._session.prefills == 2  # one per sample, every later token is incremental
+
+
+def test_flash_attention_eligibility():
+    """The tcgen05 attention takes only the plain causal case it implements; everything else
+    (masks, dropout, other head dims, ragged lengths) stays on scaled-dot-product attention."""
+    from tiny_dsv41_b200.ops import attention as A
+
+    def t(b, l, h, d, dtype=torch.bfloat16):
+        return torch.zeros(b, l, h, d, dtype=dtype)
+
+    assert A.flash_supported(t(1, 256, 8, 128), t(1, 256, 2, 128), t(1, 256, 2, 128))
+    assert not A.flash_supported(t(1, 200, 8, 128), t(1, 200, 2, 128), t(1, 200, 2, 128))  # L % 128
+    assert not A.flash_supported(t(1, 256, 8, 64), t(1, 256, 2, 64), t(1, 256, 2, 64))  # head dim
+    assert not A.flash_supported(t(1, 256, 6, 128), t(1, 256, 4, 128), t(1, 256, 4, 128))  # GQA groups
+    assert not A.flash_supported(*(t(1, 256, 4, 128, torch.float32) for _ in range(3)))  # dtype
+    q = torch.randn(1, 256, 4, 128)
+    out = A.causal_attention(q, q[:, :, :2], q[:, :, :2])  # CPU: the SDPA path
+    assert out.shape == q.shape and torch.isfinite(out).all()
