@@ -144,3 +144,34 @@ def test_qwen_head_example_runs_and_checkpoints(tmp_path):
     assert proc.returncode == 0, proc.stderr[-2000:]
     state = torch.load(tmp_path / "out" / "step-00000002.pt", weights_only=False)
     assert state["step"] == 2 and state["rollout_rng_state"].dtype == torch.uint8
+
+
+def test_admit_packet_drops_exclusions_and_stale_groups(tmp_path):
+    """Rollout packets the learner cannot train on are committed as dropped; provider exclusions
+    are also logged to excluded-groups.jsonl."""
+    import json
+    from types import SimpleNamespace
+
+    from tiny_dsv41_b200.rl.runtime import admit_packet
+
+    class Manager:
+        def __init__(self):
+            self.dropped = []
+
+        def commit(self, consumed_group_ids=(), dropped_group_ids=()):
+            self.dropped += list(dropped_group_ids)
+
+    config = SimpleNamespace(max_policy_lag=1, group_size=2)
+    manager = Manager()
+    assert admit_packet({"exclusion": {"group_id": 5, "reasons": ["bad"]}, "group_id": 5}, 3, config, manager,
+                        tmp_path) is None
+    stale = SimpleNamespace(group_id=6, policy_version=1, samples=[0, 1])
+    assert admit_packet({"group": stale}, 3, config, manager, tmp_path) is None
+    fresh = SimpleNamespace(group_id=7, policy_version=2, samples=[0, 1])
+    assert admit_packet({"group": fresh}, 3, config, manager, tmp_path) == (fresh, 1)
+    assert manager.dropped == [5, 6]
+    logged = [json.loads(line) for line in (tmp_path / "excluded-groups.jsonl").read_text().splitlines()]
+    assert logged == [{"group_id": 5, "reasons": ["bad"]}]
+    with pytest.raises(ValueError):
+        admit_packet({"group": SimpleNamespace(group_id=8, policy_version=3, samples=[0])}, 3, config, manager,
+                     tmp_path)

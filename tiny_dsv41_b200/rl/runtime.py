@@ -153,6 +153,24 @@ def _optimizer(model, config):
     return torch.optim.AdamW(params, lr=config.learning_rate, weight_decay=config.weight_decay, foreach=False)
 
 
+def admit_packet(packet: dict, step: int, config, manager, output_dir: Path):
+    """One rollout packet: (group, policy lag) when it is trainable now, or None after committing it
+    as dropped (a provider's exclusion, logged to ``excluded-groups.jsonl``, or a group whose policy
+    lag exceeds ``max_policy_lag``). A group of the wrong size is an error."""
+    if packet.get("exclusion") is not None:
+        manager.commit(dropped_group_ids=[packet["group_id"]])
+        append_jsonl(output_dir / "excluded-groups.jsonl", [packet["exclusion"]])
+        return None
+    group = packet["group"]
+    lag = policy_lag(step, group.policy_version, config.max_policy_lag)
+    if lag is None:
+        manager.commit(dropped_group_ids=[group.group_id])
+        return None
+    if len(group.samples) != config.group_size:
+        raise ValueError("incomplete group")
+    return group, lag
+
+
 def run_training(*, model_dir, data_path, config: RLConfig, random_init=False, resume=None, eval_data_path=None,
                  rollout_factory=None):
     config.validate()
@@ -255,19 +273,11 @@ def run_training(*, model_dir, data_path, config: RLConfig, random_init=False, r
                         packet = manager.get(timeout=0.2)
                     except queue.Empty:
                         continue
-                    if packet.get("exclusion") is not None:  # a provider that rejected the group
+                    admitted = admit_packet(packet, step, config, manager, output_dir)
+                    if admitted is None:
                         dropped += 1
-                        manager.commit(dropped_group_ids=[packet["group_id"]])
-                        append_jsonl(output_dir / "excluded-groups.jsonl", [packet["exclusion"]])
                         continue
-                    group = packet["group"]
-                    lag = policy_lag(step, group.policy_version, config.max_policy_lag)
-                    if lag is None:
-                        dropped += 1
-                        manager.commit(dropped_group_ids=[group.group_id])
-                        continue
-                    if len(group.samples) != config.group_size:
-                        raise ValueError("incomplete group")
+                    group, lag = admitted
                     groups.append(group)
                     packets.append(packet)
                     lags.append(lag)
