@@ -38,6 +38,17 @@ def run_reference_arm(args, metric: str, model_name: str):
 
     if args.layers != 48:
         model_name = f"REDUCED {args.layers}L (not the benchmark)"
+    # A one-GPU run is started without torchrun: give the reference's runtime the single-rank
+    # environment it reads, and open the process group here with a bounded timeout so a rank that
+    # fails (for instance out of memory) ends its peers' next collective with an error, not a hang.
+    for key, value in (("RANK", "0"), ("LOCAL_RANK", "0"), ("WORLD_SIZE", "1"), ("MASTER_ADDR", "127.0.0.1"),
+                       ("MASTER_PORT", "29533")):
+        os.environ.setdefault(key, value)
+    if not dist.is_initialized():
+        import datetime
+
+        torch.cuda.set_device(int(os.environ["LOCAL_RANK"]))
+        dist.init_process_group(backend="nccl", timeout=datetime.timedelta(seconds=300))
     runtime = initialize_runtime(require_distributed=True)
     world = runtime.world_size
     try:
@@ -46,7 +57,8 @@ def run_reference_arm(args, metric: str, model_name: str):
         config = Qwen3MoeConfig(num_hidden_layers=args.layers, max_window_layers=args.layers)
         with torch.device("meta"):
             model = Qwen3MoeForCausalLM(config, ContextParallel(None), dispatcher)
-        model = model.to_empty(device=runtime.device).to(torch.bfloat16)
+        # bf16 storage from the start, as the stock loader (load_qwen3_moe with dtype=bf16) assigns it
+        model = model.to(torch.bfloat16).to_empty(device=runtime.device)
         gen = torch.Generator(device="cuda")
         gen.manual_seed(1 + runtime.rank)
         with torch.no_grad():
