@@ -33,6 +33,9 @@ void maybe_install_segv_handler() {
 namespace tdsv {
 // status
 int64_t read_status();
+at::Tensor status_word();
+void set_peer_wait_limit_ns(int64_t ns);
+uint64_t peer_wait_limit_ns();
 // norm.cu
 std::vector<at::Tensor> moe_route_plan(const at::Tensor& ids, int64_t num_experts, int64_t block,
                                        const c10::optional<at::Tensor>& slab_counts, int64_t slab);
@@ -131,6 +134,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "tiny_dsv41_b200 sm_100a kernels";
   maybe_install_segv_handler();
   m.def("read_status", &tdsv::read_status, "read and clear the device pipeline status word");
+  m.def("status_word", &tdsv::status_word, "the current device's status word as a 1-element int32 tensor view");
+  m.def("set_peer_wait_limit_ns", &tdsv::set_peer_wait_limit_ns, "limit of waits on other ranks' flags (ns)");
+  m.def("peer_wait_limit_ns", []() { return static_cast<int64_t>(tdsv::peer_wait_limit_ns()); });
   m.def("moe_route_plan", &tdsv::moe_route_plan, "expert-major routing plan (stable, 128-row segments)",
         py::arg("ids"), py::arg("num_experts"), py::arg("block") = 128, py::arg("slab_counts") = py::none(),
         py::arg("slab") = 1);

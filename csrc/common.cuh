@@ -44,6 +44,7 @@ enum StatusCode : int {
 
 
 int* status_word_ptr();  // device pointer of the process-wide status word (defined in status.cu)
+uint64_t peer_wait_limit_ns();  // runtime limit of waits on other ranks' flags (set_peer_wait_limit_ns)
 void check_status(const char* what);  // host: read, reset and raise if non-zero
 
 __device__ __forceinline__ void report_status(int* status, int code) {

@@ -32,13 +32,14 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // Wait until flags[s] >= epoch for every s != skip (or all s). One thread per source.
-__global__ void wait_flags_kernel(const uint32_t* __restrict__ flags, int ep, uint32_t epoch, int* status) {
+__global__ void wait_flags_kernel(const uint32_t* __restrict__ flags, int ep, uint32_t epoch, int* status,
+                                  uint64_t limit_ns) {
   const int s = threadIdx.x;
   if (s >= ep) return;
   const uint64_t start = global_timer_ns();
   for (uint32_t i = 0;; ++i) {
     if (static_cast<int32_t>(ld_acquire_sys(flags + s) - epoch) >= 0) return;
-    if ((i & 63u) == 63u && global_timer_ns() - start > kWaitLimitNs) {
+    if ((i & 63u) == 63u && global_timer_ns() - start > limit_ns) {
       report_status(status, kTimeoutPeer);
       return;
     }
@@ -184,7 +185,8 @@ void ep_wait(const at::Tensor& flags, int64_t epoch) {
   TDSV_CHECK(ep <= 1024, "ep_wait: too many ranks");
   c10::cuda::CUDAGuard guard(flags.device());
   wait_flags_kernel<<<1, std::max(32, ep), 0, stream()>>>(reinterpret_cast<const uint32_t*>(flags.data_ptr()), ep,
-                                                          static_cast<uint32_t>(epoch), status_word_ptr());
+                                                          static_cast<uint32_t>(epoch), status_word_ptr(),
+                                                          peer_wait_limit_ns());
   TDSV_LAUNCH_CHECK();
 }
 

@@ -7,7 +7,24 @@ namespace {
 __device__ int g_status_word;
 constexpr int kMaxDevices = 64;
 int* g_status_ptr[kMaxDevices] = {nullptr};
+// How long a wait on another rank's flag may spin before it records kTimeoutPeer and returns.
+uint64_t g_peer_wait_limit_ns = kWaitLimitNs;
 }  // namespace
+
+uint64_t peer_wait_limit_ns() { return g_peer_wait_limit_ns; }
+
+void set_peer_wait_limit_ns(int64_t ns) {
+  TDSV_CHECK(ns > 0, "set_peer_wait_limit_ns: the limit must be positive");
+  g_peer_wait_limit_ns = static_cast<uint64_t>(ns);
+}
+
+// The status word of the current device as a one-element int32 CUDA tensor that aliases it (no
+// ownership), so the host can snapshot it asynchronously into pinned memory once per step.
+at::Tensor status_word() {
+  int dev = 0;
+  TDSV_CUDA_CHECK(cudaGetDevice(&dev));
+  return at::from_blob(status_word_ptr(), {1}, at::TensorOptions().dtype(at::kInt).device(at::kCUDA, dev));
+}
 
 int* status_word_ptr() {
   int dev = 0;

@@ -24,7 +24,9 @@
  *
  * Set-up: the first call on a device (the device current on the calling thread) looks up the
  * scratch array's device address for that device once; make that first call before any CUDA
- * stream capture begins.
+ * stream capture begins.  The address is kept for the life of the process: after
+ * cudaDeviceReset (or anything else that replaces the device's primary context) it is stale and
+ * this entry point must not be called again in that process.
  *
  * Sharing: every call on a device shares the one scratch array, and the array keeps the
  * contents of the last call.  Every scratch value a call reads is written earlier in the same

@@ -101,3 +101,40 @@ def test_corrupted_checkpoints_are_refused(tmp_path):
     Path(art["path"]).write_bytes(bytes(raw))
     with pytest.raises(ValueError):
         ck.load_policy_artifact(P(), art)
+
+
+def test_status_monitor_is_inert_without_a_gpu():
+    from tiny_dsv41_b200.ops import StatusMonitor
+
+    monitor = StatusMonitor("cpu")
+    assert not monitor.enabled
+    monitor.step_end("cpu step")  # nothing to read, nothing raised
+
+
+@pytest.mark.gpu
+def test_peer_wait_timeout_surfaces_as_a_python_error():
+    """A wait on a flag that no rank raises (one GPU, local memory) gives up after the runtime
+    limit, records status 5, and the per-step monitor raises; the context stays usable."""
+    import time
+
+    from tiny_dsv41_b200 import ops
+
+    ops.check_status("before the timeout test")
+    previous = ops.peer_wait_limit()
+    ops.set_peer_wait_limit(0.01)
+    try:
+        flags = torch.zeros(4, dtype=torch.int32, device="cuda")
+        monitor = ops.StatusMonitor("cuda")
+        start = time.perf_counter()
+        ops.ext().ep_wait(flags, 1)
+        with pytest.raises(ops.DeviceStatusError) as error:
+            monitor.step_end("timeout test")
+        assert error.value.code == 5
+        assert time.perf_counter() - start < 2.0
+        monitor.step_end("after the timeout")  # the word was reset
+        flags.fill_(1)
+        ops.ext().ep_wait(flags, 1)  # raised flags pass at once
+        monitor.step_end("raised flags")
+        assert torch.ones(8, device="cuda").sum().item() == 8
+    finally:
+        ops.set_peer_wait_limit(previous)

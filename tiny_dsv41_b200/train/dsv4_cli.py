@@ -19,6 +19,7 @@ from pathlib import Path
 import torch
 import torch.distributed as dist
 
+from ..ops import StatusMonitor
 from ..models.dsv4 import DeepSeekV41Config
 from ..parallel.cp import ContextParallel, pack_sequences
 from ..parallel.dispatch import TokenDispatcher
@@ -136,6 +137,7 @@ def train(args, runtime) -> dict:
     generator = torch.Generator(device=runtime.device)
     generator.manual_seed(args.seed + runtime.rank // args.cp_size)
     loss_v = aux_v = 0.0
+    monitor = StatusMonitor(runtime.device)
     for step in range(1, args.steps + 1):
         trace_point("step_begin", step=step)
         ids = torch.randint(3, model.config.vocab_size, (args.batch_size, args.seq_len), device=runtime.device,
@@ -163,6 +165,7 @@ def train(args, runtime) -> dict:
             optimizer.step()
         loss_v = distributed_mean(out.loss, runtime)
         aux_v = distributed_mean(out.aux_loss, runtime)
+        monitor.step_end(f"step {step}")
         trace_point("step_end", step=step, loss=loss_v)
         if runtime.is_main:
             print(json.dumps({"step": step, "loss": loss_v, "aux_loss": aux_v}), flush=True)

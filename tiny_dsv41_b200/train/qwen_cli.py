@@ -17,6 +17,7 @@ from pathlib import Path
 import torch
 import torch.distributed as dist
 
+from ..ops import StatusMonitor
 from ..models.qwen import Qwen3MoeConfig, load_qwen3_moe
 from ..parallel.cp import ContextParallel
 from ..parallel.dispatch import TokenDispatcher
@@ -99,6 +100,7 @@ def train(args, runtime) -> dict:
     tracked = model.model.layers[0].self_attn.q_proj.weight
     before = local_tensor(tracked).detach().float().clone()
     loss_v = aux_v = norm_v = 0.0
+    monitor = StatusMonitor(runtime.device)
     for step in range(1, args.steps + 1):
         trace_point("step_begin", step=step)
         ids = torch.randint(0, model.config.vocab_size, (args.batch_size, args.seq_len), device=runtime.device,
@@ -116,6 +118,7 @@ def train(args, runtime) -> dict:
         if isinstance(out.aux_loss, torch.Tensor):
             aux_v = distributed_mean(out.aux_loss, runtime)
         norm_v = float(norm)
+        monitor.step_end(f"step {step}")
         trace_point("step_end", step=step, loss=loss_v, grad_norm=norm_v)
         if runtime.is_main:
             print(json.dumps({"step": step, "loss": loss_v, "aux_loss": aux_v, "grad_norm": norm_v}), flush=True)

@@ -19,6 +19,8 @@ import time
 import torch
 import torch.distributed as dist
 
+from ..ops import StatusMonitor
+
 from ..models.qwen import Qwen3MoeConfig, Qwen3MoeForCausalLM
 from ..models.qwen.model import Qwen3MoeExperts
 from ..optim import FusedAdamW
@@ -74,6 +76,8 @@ class QwenTrainer:
             self._apply_fsdp(model)
         self.model = model
         dense = [p for p in model.parameters() if id(p) not in expert_ids]
+        # device status word (bounded peer waits, bounds checks) read once per step by the loops
+        self.monitor = StatusMonitor(rt.device)
         self.optimizers = [
             FusedAdamW(dense, lr=lr, betas=(0.9, 0.95), weight_decay=0.1, moment_dtype=moment_dtype, in_backward=True),
             FusedAdamW(self.expert_params, lr=lr, betas=(0.9, 0.95), weight_decay=0.1, moment_dtype=moment_dtype,
@@ -203,6 +207,7 @@ class QwenSFTBench:
             end.record()
             barrier()
         device_ms = start.elapsed_time(end)
+        t.monitor.step_end("timed steps")
         # end-to-end through the public API: H2D of inputs, D2H of the loss every step
         barrier()
         wall0 = time.perf_counter()
@@ -210,6 +215,7 @@ class QwenSFTBench:
         for i in range(a.steps):
             loss = t.train_step(*batches[i % len(batches)])
             e2e_losses.append(loss.item())
+            t.monitor.step_end("train_step")
         torch.cuda.synchronize()
         wall_s = time.perf_counter() - wall0
         peak_gib = torch.cuda.max_memory_allocated(rt.device) / 2 ** 30

@@ -28,6 +28,7 @@ from pathlib import Path
 import torch
 import torch.distributed as dist
 
+from ..ops import StatusMonitor
 from ..lora import LoRAConfig, adapter_parameters, inject_lora, save_adapter
 from ..parallel.fsdp import scale_expert_grads
 from ..rl.checkpoint import run_identity
@@ -347,6 +348,7 @@ def train(args, runtime) -> dict:
     emit({"event": "loaded", "step": step, "eval_loss_before": before, "generation_before": gen_before,
           "load_seconds": load_seconds})
     saved = None
+    monitor = StatusMonitor(runtime.device)
     loop_started = time.perf_counter()
     for step in range(initial + 1, args.steps + 1):
         batches, next_cursor = make_batches(examples, cursor, count=args.gradient_accumulation_steps, **options)
@@ -356,6 +358,7 @@ def train(args, runtime) -> dict:
                                ep_size=args.ep_size)
         if runtime.device.type == "cuda":
             torch.cuda.synchronize(runtime.device)
+        monitor.step_end(f"SFT step {step}")
         metrics.update(_step_resources(model, runtime, time.perf_counter() - t0))
         trace_point("step_end", step=step, seconds=metrics["seconds"])
         cursor = next_cursor
