@@ -46,7 +46,11 @@ setup(
     packages=["tiny_dsv41_b200", "tiny_dsv41_b200.models", "tiny_dsv41_b200.models.dsv4",
               "tiny_dsv41_b200.models.qwen", "tiny_dsv41_b200.ops", "tiny_dsv41_b200.optim",
               "tiny_dsv41_b200.parallel", "tiny_dsv41_b200.rl", "tiny_dsv41_b200.rollout", "tiny_dsv41_b200.train",
-              "tiny_dsv41_b200.utils"],
+              "tiny_dsv41_b200.utils",
+              # drop-in module paths of the original packages (compat/): dsv41_train.*, rollout_manager.*
+              "dsv41_train", "dsv41_train.rl", "rollout_manager"],
+    package_dir={"dsv41_train": "compat/dsv41_train", "dsv41_train.rl": "compat/dsv41_train/rl",
+                 "rollout_manager": "compat/rollout_manager"},
     package_data={"tiny_dsv41_b200.models.dsv4": ["tiny_config.json"]},
     entry_points={"console_scripts": [
         "rollout-manager = tiny_dsv41_b200.rollout.cli:main",
