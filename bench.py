@@ -41,6 +41,8 @@ def parse_args(argv=None):
     p.add_argument("--impl", choices=("native", "reference"), default="native")
     p.add_argument("--seq-len", type=int, default=4096)
     p.add_argument("--batch-size", type=int, default=1)
+    p.add_argument("--cp", type=int, default=1,
+                   help="context-parallel degree (BASELINE config 4: --cp 2 --seq-len 32768 on 4 GPUs, EP = N)")
     p.add_argument("--layers", type=int, default=48, help="development only: fewer layers is not the benchmark")
     p.add_argument("--dispatcher", choices=("auto", "nccl", "nvlink"), default="auto")
     p.add_argument("--moment-dtype", choices=("auto", "fp32", "bf16"), default="auto",

@@ -40,6 +40,7 @@
 #include "common.cuh"
 #include "tc_util.cuh"
 
+#include <cstring>
 #include <mutex>
 
 namespace tdsv {
@@ -69,6 +70,21 @@ enum : int {
     if (tracing && (it) < 64) trace[(event) * 64 + (it)] = clock64() - t0; \
   } while (0)
 
+// Where the keys and values are. Keys are numbered globally; key tile j (128 keys) belongs to
+// owner j * 128 / chunk and starts at row b * chunk + (j * 128 mod chunk) of that owner's
+// [B, chunk, Hkv, 128] tensors. One owner holding the whole sequence (chunk = L, q_offset = 0)
+// is plain causal attention; under context parallelism owner c is CP rank c, whose tensors are
+// reached through its peer mapping, and this rank's queries start at global position q_offset.
+constexpr int kMaxOwners = 8;
+struct KvMaps {
+  CUtensorMap k[kMaxOwners];
+  CUtensorMap v[kMaxOwners];
+  int chunk;     // keys per owner and batch row (a multiple of 128)
+  int q_offset;  // global position of this rank's first query (a multiple of 128)
+  __device__ __forceinline__ int owner(int j) const { return j * kTile / chunk; }
+  __device__ __forceinline__ int row(int b, int j) const { return b * chunk + j * kTile - owner(j) * chunk; }
+};
+
 // =============================================================================================
 // Forward
 // =============================================================================================
@@ -95,8 +111,7 @@ constexpr int kFwdThreads = 320;  // TMA warp, MMA warp, 8 softmax warps
 constexpr uint32_t kFwdColQ = 3 * kTile;  // TMEM: S0 [0, 128), S1 [128, 256), O [256, 384), Q [384, 448)
 
 __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_constant__ CUtensorMap tq,
-                                                          const __grid_constant__ CUtensorMap tk,
-                                                          const __grid_constant__ CUtensorMap tv,
+                                                          const __grid_constant__ KvMaps kv,
                                                           __nv_bfloat16* __restrict__ out, float* __restrict__ lse,
                                                           int seq, int heads, int kv_heads, float scale_log2,
                                                           int* __restrict__ status, long long* __restrict__ trace) {
@@ -111,7 +126,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
   const int qi = n_q - 1 - static_cast<int>(blockIdx.y);  // longest causal rows in the first wave
   const int b = blockIdx.z;
   const int hk = h / (heads / kv_heads);
-  const int n_kv = qi + 1;
+  const int gq = kv.q_offset / kTile + qi;  // global query tile: keys [0, (gq + 1) * 128) are visible
+  const int n_kv = gq + 1;
   const int row0 = b * seq + qi * kTile;
 
   if (threadIdx.x == 0) {
@@ -142,25 +158,26 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
   if (warp == 0) {
     if (elect_one()) {
       tma_prefetch_desc(&tq);
-      tma_prefetch_desc(&tk);
-      tma_prefetch_desc(&tv);
       mbar_arrive_expect_tx(&sm.q_full, 2 * kAtom);
       tma_load_3d(sm.q, &tq, &sm.q_full, 0, h, row0);
       tma_load_3d(sm.q + kAtom, &tq, &sm.q_full, 64, h, row0);
       // K_j's slot frees when S_{j-2} completes, V_j's when PV_{j-2} does: separate barriers let the
-      // next K tile load while the softmax of the current one still holds V
+      // next K tile load while the softmax of the current one still holds V. Key tile j lives in
+      // the chunk of its owner (another rank's memory under context parallelism: a plain TMA load
+      // over NVLink, never a multicast one).
       for (int j = 0; j < n_kv; ++j) {
         const int s = j & 1;
-        const int key0 = b * seq + j * kTile;
+        const int owner = kv.owner(j);
+        const int key0 = kv.row(b, j);
         if (j >= 2 && !mbar_sleep_wait(&sm.k_empty[s], ((j >> 1) - 1) & 1, status, kFwdWaitKvEmpty)) break;
         mbar_arrive_expect_tx(&sm.k_full[s], 2 * kAtom);
-        tma_load_3d(sm.k[s], &tk, &sm.k_full[s], 0, hk, key0);
-        tma_load_3d(sm.k[s] + kAtom, &tk, &sm.k_full[s], 64, hk, key0);
+        tma_load_3d(sm.k[s], &kv.k[owner], &sm.k_full[s], 0, hk, key0);
+        tma_load_3d(sm.k[s] + kAtom, &kv.k[owner], &sm.k_full[s], 64, hk, key0);
         TDSV_TRACE(0, j);
         if (j >= 2 && !mbar_sleep_wait(&sm.v_empty[s], ((j >> 1) - 1) & 1, status, kFwdWaitKvEmpty)) break;
         mbar_arrive_expect_tx(&sm.v_full[s], 2 * kAtom);
-        tma_load_3d(sm.v[s], &tv, &sm.v_full[s], 0, hk, key0);
-        tma_load_3d(sm.v[s] + kAtom, &tv, &sm.v_full[s], 64, hk, key0);
+        tma_load_3d(sm.v[s], &kv.v[owner], &sm.v_full[s], 0, hk, key0);
+        tma_load_3d(sm.v[s] + kAtom, &kv.v[owner], &sm.v_full[s], 64, hk, key0);
         TDSV_TRACE(1, j);
       }
     }
@@ -220,7 +237,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
     const int quarter = warp & 3, half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const int q_pos = qi * kTile + r;
+    const int q_pos = gq * kTile + r;  // global position (keys are numbered globally too)
     float m_used = -INFINITY, l = 0.f;
     // copy this thread's half of Q row r (64 dims, one swizzle atom row) into tensor memory
     bool ok = warp_wait(&sm.q_full, 0, status, kFwdWaitQ);
@@ -255,7 +272,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
       // causal mask on the diagonal tile, then the maximum of the raw scores (8 independent
       // chains; the scale is positive, so it is applied once to the maximum)
       const int key0 = j * kTile + half * 64;
-      if (j == qi) {
+      if (j == gq) {
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
@@ -345,7 +362,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
         }
       }
       if (half == 0)
-        lse[(static_cast<int64_t>(b) * heads + h) * seq + q_pos] = (m_used + log2f(l_row)) * 0.69314718055994531f;
+        lse[(static_cast<int64_t>(b) * heads + h) * seq + qi * kTile + r] =
+            (m_used + log2f(l_row)) * 0.69314718055994531f;
     }
   }
   tc_fence_before();
@@ -412,24 +430,34 @@ __device__ __forceinline__ void drain_reduce(uint32_t taddr, int chunks, uint8_t
 constexpr int kBwdThreads = 320;  // TMA warp, MMA warp, 8 compute warps
 constexpr int kBwdLoadWarp = 1, kBwdMmaWarp = 0;
 
+// fp32 dK / dV accumulators per key owner ([B, chunk, Hkv, 128] each): this rank's own
+// accumulators for its keys, and under context parallelism one local outbox slot per other owner,
+// which that owner sums when it finalises its gradients.
+struct AccMaps {
+  CUtensorMap dk[kMaxOwners];
+  CUtensorMap dv[kMaxOwners];
+};
+
 __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(
-    const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-    const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-    const __grid_constant__ CUtensorMap tdk_acc, const __grid_constant__ CUtensorMap tdv_acc,
-    float* __restrict__ dq_acc, const float* __restrict__ lse2, const float* __restrict__ dvec, int seq, int heads,
-    int kv_heads, float scale_log2, int* __restrict__ status, long long* __restrict__ trace) {
+    const __grid_constant__ CUtensorMap tq, const __grid_constant__ KvMaps kv, const __grid_constant__ CUtensorMap tdo,
+    const __grid_constant__ AccMaps acc_maps, float* __restrict__ dq_acc, const float* __restrict__ lse2,
+    const float* __restrict__ dvec, int seq, int heads, int kv_heads, float scale_log2, int* __restrict__ status,
+    long long* __restrict__ trace) {
   const long long t0 = clock64();
   const bool tracing = trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
   extern __shared__ uint8_t smem_raw[];
   BwdSmem& sm = *reinterpret_cast<BwdSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.x;
-  const int j = blockIdx.y;  // key tile; j = 0 sees every query block, so it is scheduled first
+  const int j = blockIdx.y;  // global key tile; j = 0 sees every query block, so it is scheduled first
   const int b = blockIdx.z;
   const int hk = h / (heads / kv_heads);
-  const int i0 = j * (kTile / kQBlk);
+  // this rank's 64-query blocks (local index) that see key tile j: from the block holding global
+  // position j * 128 (or the first local block) to the end
+  const int i0 = max(j * (kTile / kQBlk), kv.q_offset / kQBlk) - kv.q_offset / kQBlk;
   const int n_it = seq / kQBlk - i0;
-  const int key0 = b * seq + j * kTile;
+  const int owner = kv.owner(j);
+  const int key0 = kv.row(b, j);
   const int64_t stat_row = (static_cast<int64_t>(b) * heads + h) * seq;
 
   if (threadIdx.x == 0) {
@@ -462,14 +490,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(
   if (warp == kBwdLoadWarp) {
     if (elect_one()) {
       tma_prefetch_desc(&tq);
-      tma_prefetch_desc(&tk);
-      tma_prefetch_desc(&tv);
       tma_prefetch_desc(&tdo);
       mbar_arrive_expect_tx(&sm.kv_full, 4 * kAtom);
-      tma_load_3d(sm.k, &tk, &sm.kv_full, 0, hk, key0);
-      tma_load_3d(sm.k + kAtom, &tk, &sm.kv_full, 64, hk, key0);
-      tma_load_3d(sm.v, &tv, &sm.kv_full, 0, hk, key0);
-      tma_load_3d(sm.v + kAtom, &tv, &sm.kv_full, 64, hk, key0);
+      tma_load_3d(sm.k, &kv.k[owner], &sm.kv_full, 0, hk, key0);
+      tma_load_3d(sm.k + kAtom, &kv.k[owner], &sm.kv_full, 64, hk, key0);
+      tma_load_3d(sm.v, &kv.v[owner], &sm.kv_full, 0, hk, key0);
+      tma_load_3d(sm.v + kAtom, &kv.v[owner], &sm.kv_full, 64, hk, key0);
       for (int it = 0; it < n_it; ++it) {
         const int s = it % kQStages;
         if (it >= kQStages && !mbar_sleep_wait(&sm.q_empty[s], ((it / kQStages) - 1) & 1, status, kBwdWaitQEmpty)) break;
@@ -579,7 +605,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(
     const int quarter = warp & 3, half = (warp - 2) >> 2;
     const int r = quarter * 32 + lane;
     const uint32_t lane_addr = tmem + (static_cast<uint32_t>(quarter * 32) << 16);
-    const int key_pos = j * kTile + r;
+    const int key_pos = j * kTile + r;  // global
     // dQ^T drain: 32 queries of dim r, added to dq_acc [B, L, H, 128] (a warp covers 32 adjacent dims)
     auto drain_dq = [&](int it) {
       uint32_t v[32];
@@ -594,7 +620,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(
     bool ok = true;
     for (int it = 0; it < n_it; ++it) {
       const int s = it & 1;
-      const int q0 = (i0 + it) * kQBlk + half * 32;  // first query of this thread's half
+      const int q0 = kv.q_offset + (i0 + it) * kQBlk + half * 32;  // first (global) query of this thread's half
       const int st = it % kQStages;
       if (!(ok = warp_wait(&sm.q_full[st], (it / kQStages) & 1, status, kBwdWaitQc))) break;
       if (!(ok = warp_wait(&sm.s_full[s], (it >> 1) & 1, status, kBwdWaitS))) break;
@@ -661,11 +687,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1) attn_bwd_kernel(
       tc_fence_after();
       drain_dq(n_it - 1);
       uint8_t* box = sm.q[0] + (warp - 2) * 4096;
-      const int row = b * seq + j * kTile + quarter * 32;
+      const int row = key0 + quarter * 32;
+      const CUtensorMap* tdk = &acc_maps.dk[owner];
+      const CUtensorMap* tdv = &acc_maps.dv[owner];
       drain_reduce(lane_addr + kColDk + half * 64, 2, box, lane,
-                   [&](uint32_t src, int c) { tma_reduce_add_3d(&tdk_acc, src, half * 64 + c * 32, hk, row); });
+                   [&](uint32_t src, int c) { tma_reduce_add_3d(tdk, src, half * 64 + c * 32, hk, row); });
       drain_reduce(lane_addr + kColDv + half * 64, 2, box, lane,
-                   [&](uint32_t src, int c) { tma_reduce_add_3d(&tdv_acc, src, half * 64 + c * 32, hk, row); });
+                   [&](uint32_t src, int c) { tma_reduce_add_3d(tdv, src, half * 64 + c * 32, hk, row); });
     }
     if (lane == 0) bulk_wait_group0();  // reductions complete before the CTA exits
     __syncwarp();
@@ -733,24 +761,46 @@ __global__ void attn_bwd_finalize_kernel(const float* __restrict__ acc, __nv_bfl
 // ---------------------------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------------------------
-// Token-major [tokens, heads, 128] tensor, box {64 bf16 or 32 fp32 columns, 1 head, box_rows tokens}.
-CUtensorMap head_major_map(const at::Tensor& t, int heads, int box_rows) {
+// Token-major [tokens, heads, 128] array at `base`, box {64 bf16 or 32 fp32 columns, 1 head, box_rows tokens}.
+CUtensorMap head_major_map(void* base, bool bf16, int64_t tokens, int heads, int box_rows) {
   bind_primary_context();
-  const bool bf16 = t.scalar_type() == at::kBFloat16;
   const int esize = bf16 ? 2 : 4;
-  TDSV_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, "attention tensor base must be 16-byte aligned");
-  const int64_t tokens = t.numel() / (static_cast<int64_t>(heads) * kDim);
+  TDSV_CHECK(reinterpret_cast<uintptr_t>(base) % 16 == 0, "attention tensor base must be 16-byte aligned");
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(kDim), static_cast<cuuint64_t>(heads), static_cast<cuuint64_t>(tokens)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(kDim) * esize, static_cast<cuuint64_t>(heads) * kDim * esize};
   cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / esize), 1, static_cast<cuuint32_t>(box_rows)};
   cuuint32_t estr[3] = {1, 1, 1};
   CUtensorMap map;
   CUresult r = encode_fn()(&map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3,
-                           t.data_ptr(), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code ", static_cast<int>(r));
   return map;
+}
+
+CUtensorMap head_major_map(const at::Tensor& t, int heads, int box_rows) {
+  return head_major_map(t.data_ptr(), t.scalar_type() == at::kBFloat16, t.numel() / (static_cast<int64_t>(heads) * kDim),
+                        heads, box_rows);
+}
+
+// K / V sources: owner c's [B, chunk, Hkv, 128] bf16 tensors at k_ptrs[c] / v_ptrs[c].
+KvMaps kv_maps(const std::vector<int64_t>& k_ptrs, const std::vector<int64_t>& v_ptrs, int64_t batch, int64_t chunk,
+               int kv_heads, int64_t q_offset, int box_rows) {
+  TDSV_CHECK(!k_ptrs.empty() && k_ptrs.size() == v_ptrs.size() && k_ptrs.size() <= kMaxOwners,
+             "attention: 1 to 8 key / value owners");
+  TDSV_CHECK(chunk > 0 && chunk % kTile == 0 && q_offset % kTile == 0 && q_offset >= 0,
+             "attention: the key chunk and the query offset must be multiples of 128");
+  TDSV_CHECK(batch * chunk <= (1 << 30), "attention: too many keys per owner");
+  KvMaps m;
+  std::memset(&m, 0, sizeof(m));
+  for (size_t c = 0; c < k_ptrs.size(); ++c) {
+    m.k[c] = head_major_map(reinterpret_cast<void*>(k_ptrs[c]), true, batch * chunk, kv_heads, box_rows);
+    m.v[c] = head_major_map(reinterpret_cast<void*>(v_ptrs[c]), true, batch * chunk, kv_heads, box_rows);
+  }
+  m.chunk = static_cast<int>(chunk);
+  m.q_offset = static_cast<int>(q_offset);
+  return m;
 }
 
 void check_operands(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v) {
@@ -771,6 +821,22 @@ void set_smem(Kernel kernel, size_t bytes) {
   TDSV_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
 }
 
+void launch_fwd(const at::Tensor& q, const KvMaps& kv, int kv_heads, at::Tensor& out, at::Tensor& lse,
+                long long* trace_ptr) {
+  const int64_t batch = q.size(0), seq = q.size(1);
+  const int heads = static_cast<int>(q.size(2));
+  const CUtensorMap mq = head_major_map(q, heads, kTile);
+  const size_t smem = sizeof(FwdSmem) + 1024;
+  static std::once_flag once;
+  std::call_once(once, [&] { set_smem(attn_fwd_kernel, smem); });
+  dim3 grid(static_cast<unsigned>(heads), static_cast<unsigned>(seq / kTile), static_cast<unsigned>(batch));
+  attn_fwd_kernel<<<grid, kFwdThreads, smem, stream()>>>(mq, kv, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                                                         lse.data_ptr<float>(), static_cast<int>(seq), heads, kv_heads,
+                                                         kLog2e / sqrtf(static_cast<float>(kDim)),
+                                                         status_word_ptr(), trace_ptr);
+  TDSV_LAUNCH_CHECK();
+}
+
 }  // namespace
 
 // q [B, L, H, 128], k/v [B, L, Hkv, 128] bf16 -> (out [B, L, H, 128] bf16, lse [B, H, L] fp32)
@@ -789,18 +855,105 @@ std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const
   auto lse = at::empty({batch, heads, seq}, q.options().dtype(at::kFloat));
   if (batch == 0 || seq == 0) return {out, lse};
   c10::cuda::CUDAGuard guard(q.device());
-  const CUtensorMap mq = head_major_map(q, heads, kTile), mk = head_major_map(k, kv_heads, kTile),
-                    mv = head_major_map(v, kv_heads, kTile);
-  const size_t smem = sizeof(FwdSmem) + 1024;
-  static std::once_flag once;
-  std::call_once(once, [&] { set_smem(attn_fwd_kernel, smem); });
-  dim3 grid(static_cast<unsigned>(heads), static_cast<unsigned>(seq / kTile), static_cast<unsigned>(batch));
-  attn_fwd_kernel<<<grid, kFwdThreads, smem, stream()>>>(mq, mk, mv, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-                                                 lse.data_ptr<float>(), static_cast<int>(seq), heads, kv_heads,
-                                                 kLog2e / sqrtf(static_cast<float>(kDim)), status_word_ptr(), trace_ptr);
-  TDSV_LAUNCH_CHECK();
+  launch_fwd(q, kv_maps({reinterpret_cast<int64_t>(k.data_ptr())}, {reinterpret_cast<int64_t>(v.data_ptr())}, batch,
+                        seq, kv_heads, 0, kTile),
+             kv_heads, out, lse, trace_ptr);
   return {out, lse};
 }
+
+// Context-parallel forward: this rank's queries q [B, Lq, H, 128] start at global position q_offset;
+// keys / values are split into chunks of `chunk` positions, chunk c at k_ptrs[c] / v_ptrs[c]
+// ([B, chunk, Hkv, 128] bf16; another rank's memory reached through its peer mapping). Tiles of
+// other ranks are read by plain (non-multicast) TMA loads straight into the softmax pipeline.
+std::vector<at::Tensor> attn_fwd_cp(const at::Tensor& q, const std::vector<int64_t>& k_ptrs,
+                                    const std::vector<int64_t>& v_ptrs, int64_t chunk, int64_t q_offset,
+                                    int64_t kv_heads) {
+  check_cuda_tensor(q, "attention q");
+  TDSV_CHECK(q.scalar_type() == at::kBFloat16 && q.dim() == 4 && q.size(3) == kDim && q.size(1) % kTile == 0,
+             "attention: bf16 q [B, L, H, 128] with L a multiple of 128");
+  TDSV_CHECK(kv_heads > 0 && q.size(2) % kv_heads == 0, "attention: query heads must be a multiple of kv heads");
+  TDSV_CHECK((q_offset + q.size(1) + chunk - 1) / chunk <= static_cast<int64_t>(k_ptrs.size()),
+             "attention: the visible keys need more owners than given");
+  const int64_t batch = q.size(0), seq = q.size(1);
+  auto out = at::empty_like(q);
+  auto lse = at::empty({batch, q.size(2), seq}, q.options().dtype(at::kFloat));
+  if (batch == 0 || seq == 0) return {out, lse};
+  c10::cuda::CUDAGuard guard(q.device());
+  launch_fwd(q, kv_maps(k_ptrs, v_ptrs, batch, chunk, static_cast<int>(kv_heads), q_offset, kTile),
+             static_cast<int>(kv_heads), out, lse, nullptr);
+  return {out, lse};
+}
+
+namespace {
+
+// D / lse2 prep, the backward kernel over `n_key_tiles` global key tiles, and dq_acc -> dq (bf16).
+void launch_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& out, const at::Tensor& lse,
+                const KvMaps& kv, const AccMaps& acc, int kv_heads, int64_t n_key_tiles, float* dq_acc, float* dvec,
+                float* lse2, long long* trace_ptr) {
+  const int64_t batch = q.size(0), seq = q.size(1);
+  const int heads = static_cast<int>(q.size(2));
+  const float scale = 1.f / sqrtf(static_cast<float>(kDim));
+  const int64_t rows = batch * seq * heads;
+  attn_bwd_prep_kernel<<<static_cast<unsigned>(std::min<int64_t>((rows + 15) / 16, 148 * 16)), 256, 0, stream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
+      lse.data_ptr<float>(), dvec, lse2, rows, static_cast<int>(seq), heads);
+  TDSV_LAUNCH_CHECK();
+  const CUtensorMap mq = head_major_map(q, heads, kQBlk), mdo = head_major_map(dout, heads, kQBlk);
+  const size_t smem = sizeof(BwdSmem) + 1024;
+  static std::once_flag once;
+  std::call_once(once, [&] { set_smem(attn_bwd_kernel, smem); });
+  dim3 grid(static_cast<unsigned>(heads), static_cast<unsigned>(n_key_tiles), static_cast<unsigned>(batch));
+  attn_bwd_kernel<<<grid, kBwdThreads, smem, stream()>>>(mq, kv, mdo, acc, dq_acc, lse2, dvec, static_cast<int>(seq),
+                                                         heads, kv_heads, kLog2e * scale, status_word_ptr(), trace_ptr);
+  TDSV_LAUNCH_CHECK();
+}
+
+void check_backward_operands(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& out,
+                             const at::Tensor& lse) {
+  check_cuda_tensor(dout, "attention dout");
+  check_cuda_tensor(out, "attention out");
+  check_cuda_tensor(lse, "attention lse");
+  TDSV_CHECK(dout.sizes() == q.sizes() && out.sizes() == q.sizes() && dout.scalar_type() == at::kBFloat16 &&
+                 out.scalar_type() == at::kBFloat16,
+             "attention backward: dout / out must be bf16 shaped like q");
+  TDSV_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == q.size(0) * q.size(2) * q.size(1),
+             "attention backward: lse [B, H, L]");
+}
+
+void convert_to_bf16(const float* acc, at::Tensor& dq, at::Tensor* dk, at::Tensor* dv, float scale) {
+  const int64_t nq8 = dq.numel() / 8, nkv8 = dk != nullptr ? dk->numel() / 8 : 0;
+  attn_bwd_finalize_kernel<<<static_cast<unsigned>(std::min<int64_t>((nq8 + 2 * nkv8 + 255) / 256, 148 * 8)), 256, 0,
+                             stream()>>>(acc, reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()),
+                                         dk != nullptr ? reinterpret_cast<__nv_bfloat16*>(dk->data_ptr()) : nullptr,
+                                         dv != nullptr ? reinterpret_cast<__nv_bfloat16*>(dv->data_ptr()) : nullptr,
+                                         nq8, nkv8, scale);
+  TDSV_LAUNCH_CHECK();
+}
+
+// dk = scale * sum_r box_r[me][0], dv = sum_r box_r[me][1] over the ranks r = me .. n - 1 whose
+// queries see this rank's keys, in that fixed order; box_r is rank r's fp32 outbox
+// [n, 2, B, chunk, Hkv, 128], read over NVLink for r != me. 8 values per thread.
+__global__ void attn_cp_finalize_kernel(const int64_t* __restrict__ boxes, int n, int me, int64_t slot8,
+                                        __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv, float scale) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < 2 * slot8; i += stride) {
+    float a[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int r = me; r < n; ++r) {
+      const float4* src = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(boxes[r]) +
+                                                          (static_cast<int64_t>(me) * 2 * slot8 + i) * 8);
+      const float4 x0 = __ldcg(src), x1 = __ldcg(src + 1);
+      a[0] += x0.x; a[1] += x0.y; a[2] += x0.z; a[3] += x0.w;
+      a[4] += x1.x; a[5] += x1.y; a[6] += x1.z; a[7] += x1.w;
+    }
+    const bool is_k = i < slot8;
+    const float m = is_k ? scale : 1.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) a[q] *= m;
+    store_bf16x8((is_k ? dk + i * 8 : dv + (i - slot8) * 8), a);
+  }
+}
+
+}  // namespace
 
 // Gradients of attn_fwd: (dq, dk, dv) in the layouts of q, k, v.
 std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
@@ -813,54 +966,88 @@ std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, co
     trace_ptr = reinterpret_cast<long long*>(trace->data_ptr());
   }
   check_operands(q, k, v);
-  check_cuda_tensor(dout, "attention dout");
-  check_cuda_tensor(out, "attention out");
-  check_cuda_tensor(lse, "attention lse");
-  TDSV_CHECK(dout.sizes() == q.sizes() && out.sizes() == q.sizes() && dout.scalar_type() == at::kBFloat16 &&
-                 out.scalar_type() == at::kBFloat16,
-             "attention backward: dout / out must be bf16 shaped like q");
+  check_backward_operands(dout, q, out, lse);
   const int64_t batch = q.size(0), seq = q.size(1);
   const int heads = static_cast<int>(q.size(2)), kv_heads = static_cast<int>(k.size(2));
-  TDSV_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == batch * heads * seq, "attention backward: lse [B, H, L]");
   auto dq = at::empty_like(q), dk = at::empty_like(k), dv = at::empty_like(v);
   if (batch == 0 || seq == 0) return {dq, dk, dv};
   c10::cuda::CUDAGuard guard(q.device());
-  const float scale = 1.f / sqrtf(static_cast<float>(kDim));
   // one fp32 workspace: dq_acc [B, L, H, 128], dk_acc, dv_acc [B, L, Hkv, 128], then D and lse2 [B, H, L]
   const int64_t n_q = q.numel(), n_kv = k.numel(), n_stat = batch * heads * seq;
   auto ws = at::empty({n_q + 2 * n_kv + 2 * n_stat}, q.options().dtype(at::kFloat));
   TDSV_CUDA_CHECK(cudaMemsetAsync(ws.data_ptr(), 0, (n_q + 2 * n_kv) * sizeof(float), stream()));
   float* dq_acc = ws.data_ptr<float>();
-  auto dk_acc = ws.narrow(0, n_q, n_kv).view(k.sizes());
-  auto dv_acc = ws.narrow(0, n_q + n_kv, n_kv).view(k.sizes());
   float* dvec = dq_acc + n_q + 2 * n_kv;
-  float* lse2 = dvec + n_stat;
-
-  const int64_t rows = batch * seq * heads;
-  attn_bwd_prep_kernel<<<static_cast<unsigned>(std::min<int64_t>((rows + 15) / 16, 148 * 16)), 256, 0, stream()>>>(
-      reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr()),
-      lse.data_ptr<float>(), dvec, lse2, rows, static_cast<int>(seq), heads);
-  TDSV_LAUNCH_CHECK();
-
-  const CUtensorMap mq = head_major_map(q, heads, kQBlk), mdo = head_major_map(dout, heads, kQBlk);
-  const CUtensorMap mk = head_major_map(k, kv_heads, kTile), mv = head_major_map(v, kv_heads, kTile);
-  const CUtensorMap mdk = head_major_map(dk_acc, kv_heads, 32), mdv = head_major_map(dv_acc, kv_heads, 32);
-  const size_t smem = sizeof(BwdSmem) + 1024;
-  static std::once_flag once;
-  std::call_once(once, [&] { set_smem(attn_bwd_kernel, smem); });
-  dim3 grid(static_cast<unsigned>(heads), static_cast<unsigned>(seq / kTile), static_cast<unsigned>(batch));
-  attn_bwd_kernel<<<grid, kBwdThreads, smem, stream()>>>(mq, mk, mv, mdo, mdk, mdv, dq_acc, lse2, dvec,
-                                                         static_cast<int>(seq), heads, kv_heads, kLog2e * scale,
-                                                         status_word_ptr(), trace_ptr);
-  TDSV_LAUNCH_CHECK();
-
-  const int64_t nq8 = n_q / 8, nkv8 = n_kv / 8;
-  attn_bwd_finalize_kernel<<<static_cast<unsigned>(std::min<int64_t>((nq8 + 2 * nkv8 + 255) / 256, 148 * 8)), 256, 0,
-                             stream()>>>(dq_acc, reinterpret_cast<__nv_bfloat16*>(dq.data_ptr()),
-                                         reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()),
-                                         reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()), nq8, nkv8, scale);
-  TDSV_LAUNCH_CHECK();
+  AccMaps acc;
+  std::memset(&acc, 0, sizeof(acc));
+  acc.dk[0] = head_major_map(dq_acc + n_q, false, batch * seq, kv_heads, 32);
+  acc.dv[0] = head_major_map(dq_acc + n_q + n_kv, false, batch * seq, kv_heads, 32);
+  const KvMaps kv = kv_maps({reinterpret_cast<int64_t>(k.data_ptr())}, {reinterpret_cast<int64_t>(v.data_ptr())},
+                            batch, seq, kv_heads, 0, kTile);
+  launch_bwd(dout, q, out, lse, kv, acc, kv_heads, seq / kTile, dq_acc, dvec, dvec + n_stat, trace_ptr);
+  convert_to_bf16(dq_acc, dq, &dk, &dv, 1.f / sqrtf(static_cast<float>(kDim)));
   return {dq, dk, dv};
+}
+
+// Context-parallel backward of attn_fwd_cp. Returns dq (bf16, like q). The dK / dV partial sums
+// of every key owner this rank's queries see go into `outbox` (fp32 [n_owners, 2, B, chunk, Hkv,
+// 128], this rank's local memory, zeroed here): slot c holds owner c's partials. After every
+// rank's backward has finished, owner c sums slot c of all outboxes with attn_cp_finalize.
+at::Tensor attn_bwd_cp(const at::Tensor& dout, const at::Tensor& q, const std::vector<int64_t>& k_ptrs,
+                       const std::vector<int64_t>& v_ptrs, const at::Tensor& out, const at::Tensor& lse, int64_t chunk,
+                       int64_t q_offset, int64_t kv_heads, at::Tensor& outbox) {
+  check_cuda_tensor(q, "attention q");
+  check_backward_operands(dout, q, out, lse);
+  check_cuda_tensor(outbox, "attention outbox");
+  const int64_t batch = q.size(0), seq = q.size(1);
+  const int owners = static_cast<int>(k_ptrs.size());
+  const int64_t slot = batch * chunk * kv_heads * kDim;
+  TDSV_CHECK(outbox.scalar_type() == at::kFloat && outbox.numel() >= owners * 2 * slot,
+             "attention outbox: fp32 [owners, 2, B, chunk, Hkv, 128]");
+  TDSV_CHECK((q_offset + seq + chunk - 1) / chunk <= owners, "attention: the visible keys need more owners than given");
+  const int heads = static_cast<int>(q.size(2));
+  auto dq = at::empty_like(q);
+  if (batch == 0 || seq == 0) return dq;
+  c10::cuda::CUDAGuard guard(q.device());
+  const int64_t n_q = q.numel(), n_stat = batch * heads * seq;
+  auto ws = at::empty({n_q + 2 * n_stat}, q.options().dtype(at::kFloat));
+  TDSV_CUDA_CHECK(cudaMemsetAsync(ws.data_ptr(), 0, n_q * sizeof(float), stream()));
+  TDSV_CUDA_CHECK(cudaMemsetAsync(outbox.data_ptr(), 0, owners * 2 * slot * sizeof(float), stream()));
+  float* dq_acc = ws.data_ptr<float>();
+  AccMaps acc;
+  std::memset(&acc, 0, sizeof(acc));
+  float* box = outbox.data_ptr<float>();
+  for (int c = 0; c < owners; ++c) {
+    acc.dk[c] = head_major_map(box + (2 * c) * slot, false, batch * chunk, static_cast<int>(kv_heads), 32);
+    acc.dv[c] = head_major_map(box + (2 * c + 1) * slot, false, batch * chunk, static_cast<int>(kv_heads), 32);
+  }
+  const KvMaps kv = kv_maps(k_ptrs, v_ptrs, batch, chunk, static_cast<int>(kv_heads), q_offset, kTile);
+  launch_bwd(dout, q, out, lse, kv, acc, static_cast<int>(kv_heads), (q_offset + seq) / kTile, dq_acc, dq_acc + n_q,
+             dq_acc + n_q + n_stat, nullptr);
+  convert_to_bf16(dq_acc, dq, nullptr, nullptr, 1.f / sqrtf(static_cast<float>(kDim)));
+  return dq;
+}
+
+// This rank's (dk, dv) [B, chunk, Hkv, 128] bf16 from slot `me` of the outboxes of ranks me .. n - 1
+// (`boxes`: int64 [n] device tensor of their base addresses, peer mappings for the other ranks).
+std::vector<at::Tensor> attn_cp_finalize(const at::Tensor& boxes, int64_t me, int64_t batch, int64_t chunk,
+                                         int64_t kv_heads) {
+  check_cuda_tensor(boxes, "attention outbox table");
+  TDSV_CHECK(boxes.scalar_type() == at::kLong && boxes.dim() == 1, "attention outbox table: int64 [n]");
+  const int n = static_cast<int>(boxes.numel());
+  TDSV_CHECK(me >= 0 && me < n, "attention finalize: rank out of range");
+  auto opts = boxes.options().dtype(at::kBFloat16);
+  auto dk = at::empty({batch, chunk, kv_heads, kDim}, opts), dv = at::empty({batch, chunk, kv_heads, kDim}, opts);
+  const int64_t slot8 = batch * chunk * kv_heads * kDim / 8;
+  if (slot8 == 0) return {dk, dv};
+  c10::cuda::CUDAGuard guard(boxes.device());
+  attn_cp_finalize_kernel<<<static_cast<unsigned>(std::min<int64_t>((2 * slot8 + 255) / 256, 148 * 8)), 256, 0,
+                            stream()>>>(boxes.data_ptr<int64_t>(), n, static_cast<int>(me), slot8,
+                                        reinterpret_cast<__nv_bfloat16*>(dk.data_ptr()),
+                                        reinterpret_cast<__nv_bfloat16*>(dv.data_ptr()),
+                                        1.f / sqrtf(static_cast<float>(kDim)));
+  TDSV_LAUNCH_CHECK();
+  return {dk, dv};
 }
 
 }  // namespace tdsv

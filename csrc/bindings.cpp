@@ -128,6 +128,14 @@ std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const
 std::vector<at::Tensor> attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
                                  const at::Tensor& v, const at::Tensor& out, const at::Tensor& lse,
                                  const c10::optional<at::Tensor>& trace);
+std::vector<at::Tensor> attn_fwd_cp(const at::Tensor& q, const std::vector<int64_t>& k_ptrs,
+                                    const std::vector<int64_t>& v_ptrs, int64_t chunk, int64_t q_offset,
+                                    int64_t kv_heads);
+at::Tensor attn_bwd_cp(const at::Tensor& dout, const at::Tensor& q, const std::vector<int64_t>& k_ptrs,
+                       const std::vector<int64_t>& v_ptrs, const at::Tensor& out, const at::Tensor& lse, int64_t chunk,
+                       int64_t q_offset, int64_t kv_heads, at::Tensor& outbox);
+std::vector<at::Tensor> attn_cp_finalize(const at::Tensor& boxes, int64_t me, int64_t batch, int64_t chunk,
+                                         int64_t kv_heads);
 }  // namespace tdsv
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -145,6 +153,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("k"), py::arg("v"), py::arg("trace") = py::none());
   m.def("attn_bwd", &tdsv::attn_bwd, "causal GQA flash attention backward (tcgen05): (dq, dk, dv)", py::arg("dout"),
         py::arg("q"), py::arg("k"), py::arg("v"), py::arg("out"), py::arg("lse"), py::arg("trace") = py::none());
+  m.def("attn_fwd_cp", &tdsv::attn_fwd_cp,
+        "context-parallel causal attention forward: keys / values read from each owner's chunk (peer memory)");
+  m.def("attn_bwd_cp", &tdsv::attn_bwd_cp,
+        "context-parallel attention backward: dq, with per-owner dK / dV partials in the local outbox");
+  m.def("attn_cp_finalize", &tdsv::attn_cp_finalize,
+        "this rank's dk / dv: fixed-order sum of its slot in every rank's outbox (peer loads)");
   m.def("cache_fake_quant", &tdsv::cache_fake_quant, "FP8 / FP4 block fake quantization (0 fp8, 1 fp4_index, 2 fp4_kv)");
   m.def("index_scores", &tdsv::index_scores, "DSV4 sparse-indexer scores (tcgen05, fused relu / head reduction)");
   m.def("fp4_dequant", &tdsv::fp4_dequant, "MXFP4 (E2M1 + E8M0 per 32) to bf16");

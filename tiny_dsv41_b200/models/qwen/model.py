@@ -25,6 +25,7 @@ from ... import ops
 from ...ops.router import AuxGradient
 from ...parallel import replay
 from ...parallel.cp import ContextParallel
+from ...parallel.cp_attention import fused_supported
 from ...parallel.dispatch import TokenDispatcher
 from ...utils.trace import nvtx_range
 from ..common import Linear, LMHead, fusable
@@ -47,6 +48,7 @@ class Qwen3MoeAttention(nn.Module):
         if config.head_dim != 128:
             raise ValueError("the fused QKV/RoPE kernel supports head_dim 128")
         self.layer_id = layer_id
+        self.num_layers = config.num_hidden_layers
         self.context_parallel = context_parallel
         self.num_heads = config.num_attention_heads
         self.num_key_value_heads = config.num_key_value_heads
@@ -84,6 +86,11 @@ class Qwen3MoeAttention(nn.Module):
             k, v, key_positions = cache.append(self.layer_id, k, v, position_ids)
             mask = key_positions[:, None, None, :] <= position_ids[:, None, :, None]
             out = ops.causal_attention(q, k, v, mask=mask)
+            return self.o_proj(out.reshape(batch, length, -1))
+        if cp.enabled and cp.fused_attention and cp.plain_causal and attention_mask is None and \
+                fused_supported(q, k, cp.size):
+            # K/V chunks of the other CP ranks stream over NVLink into the attention kernels
+            out = cp.fused(self.num_layers)(q, k, v, self.layer_id)
             return self.o_proj(out.reshape(batch, length, -1))
         if cp.enabled:
             k = cp.gather(k, dim=1)
@@ -210,9 +217,10 @@ class Qwen3MoeModel(nn.Module):
             raise ValueError("sequence is longer than max_position_embeddings")
         if attention_mask is not None and attention_mask.shape != input_ids.shape:
             raise ValueError("attention_mask must have the same shape as input_ids")
+        cp = self.context_parallel
+        cp.plain_causal = position_ids is None and attention_mask is None and cache is None
         if position_ids is None:
             position_ids = torch.arange(input_ids.shape[1], device=input_ids.device).unsqueeze(0).expand_as(input_ids)
-        cp = self.context_parallel
         input_ids, position_ids = cp.shard(input_ids), cp.shard(position_ids.contiguous())
         if attention_mask is not None:
             attention_mask = cp.shard(attention_mask)

@@ -95,11 +95,24 @@ class _LeftHalo(torch.autograd.Function):
 class ContextParallel:
     """Token sharding and the collectives sequence modules need under CP."""
 
-    def __init__(self, mesh: "DeviceMesh | None" = None) -> None:
+    def __init__(self, mesh: "DeviceMesh | None" = None, *, fused_attention: bool = True) -> None:
         self.mesh = mesh
         self.size = 1 if mesh is None else mesh.size()
         self.rank = 0 if mesh is None else mesh.get_local_rank()
         self.group = None if mesh is None else mesh.get_group()
+        # causal attention with the K/V exchange inside the kernels (parallel.cp_attention) for
+        # inputs with default positions and no padding mask; set per forward by the model
+        self.fused_attention = fused_attention
+        self.plain_causal = False
+        self._fused = None
+
+    def fused(self, num_layers: int):
+        """The model's fused CP attention (created on first use; CUDA only)."""
+        if self._fused is None:
+            from .cp_attention import FusedCPAttention
+
+            self._fused = FusedCPAttention(self.group, num_layers)
+        return self._fused
 
     @property
     def enabled(self) -> bool:

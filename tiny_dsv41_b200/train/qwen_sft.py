@@ -47,19 +47,22 @@ def _init_on_device(model: Qwen3MoeForCausalLM, seed: int, rank: int) -> None:
 class QwenTrainer:
     def __init__(self, config: Qwen3MoeConfig, *, lr: float = 1e-5, moment_dtype=torch.float32,
                  dispatcher: str = "auto", gradient_checkpointing: bool = True, seed: int = 0,
-                 tokens_per_rank: int = 4096) -> None:
+                 tokens_per_rank: int = 4096, cp_size: int = 1) -> None:
         self.runtime = initialize_runtime(require_distributed=int(os.environ.get("WORLD_SIZE", "1")) > 1,
                                           timeout_seconds=900)
         rt = self.runtime
         torch.manual_seed(seed)
         self.world = rt.world_size
         self.tokens_per_rank = tokens_per_rank  # sizes the NVLink receive slabs
+        self.cp_size = cp_size
         self.meshes = None
         cp = ContextParallel()
         if self.world > 1:
             from ..parallel.meshes import ParallelMeshes
 
-            self.meshes = ParallelMeshes.build(cp=1, ep=self.world)
+            self.meshes = ParallelMeshes.build(cp=cp_size, ep=self.world)
+            if cp_size > 1:  # each sequence split in cp contiguous chunks; K/V exchanged inside attention
+                cp = ContextParallel(self.meshes.cp)
             token_dispatcher = self._make_dispatcher(dispatcher)
         else:
             token_dispatcher = TokenDispatcher()
@@ -99,7 +102,10 @@ class QwenTrainer:
         from torch.distributed.fsdp import MixedPrecisionPolicy, fully_shard
 
         policy = MixedPrecisionPolicy(param_dtype=torch.bfloat16, reduce_dtype=torch.float32)
-        mesh = self.meshes.fsdp
+        # dense weights are sharded over every rank: under context parallelism the ranks of a CP
+        # group hold different tokens of one sequence, so their gradients are reduced together
+        # (the CP mean loss scales its backward by cp, which makes the world average exact)
+        mesh = self.meshes.world
         ignored = set(self.expert_params)
         # Decoder layers stay gathered from their forward to their backward: 48 layers of bf16 attention
         # and router weights are ~1.8 GB, and this saves the second all-gather per layer (the
@@ -144,8 +150,9 @@ class QwenSFTBench:
         self.args = args
         config = Qwen3MoeConfig(num_hidden_layers=args.layers, max_window_layers=args.layers)
         moment = torch.float32 if args.moment_dtype == "fp32" else torch.bfloat16
+        self.cp = getattr(args, "cp", 1)
         self.trainer = QwenTrainer(config, lr=args.lr, moment_dtype=moment, dispatcher=args.dispatcher,
-                                   tokens_per_rank=args.batch_size * args.seq_len)
+                                   tokens_per_rank=args.batch_size * args.seq_len // self.cp, cp_size=self.cp)
         self.config = config
 
     def _batch(self, gen: torch.Generator):
@@ -182,7 +189,8 @@ class QwenSFTBench:
         a = self.args
         t = self.trainer
         rt = t.runtime
-        gen = torch.Generator().manual_seed(1234 + rt.rank)
+        # the ranks of one CP group train on the same sequences (each keeps its own chunk)
+        gen = torch.Generator().manual_seed(1234 + rt.rank // self.cp)
         batches = [self._batch(gen) for _ in range(4)]
         # L2 flush buffer (larger than the 126 MB L2) written between timed steps
         flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=rt.device)
@@ -226,7 +234,7 @@ class QwenSFTBench:
         if dist.is_initialized():
             dist.all_reduce(times, op=dist.ReduceOp.MAX)
         device_ms, wall_ms, peak_gib = times.tolist()
-        tokens = a.batch_size * a.seq_len * rt.world_size * a.steps
+        tokens = a.batch_size * a.seq_len * (rt.world_size // self.cp) * a.steps
         value = tokens / (device_ms / 1000.0)
         e2e = tokens / (wall_ms / 1000.0)
         final_loss = float(losses[-1].item())
@@ -243,8 +251,9 @@ class QwenSFTBench:
             "clocks": clocks.summary(),
             "config": {
                 "model": MODEL_NAME if self.config.num_hidden_layers == 48 else f"REDUCED {self.config.num_hidden_layers}L (not the benchmark)",
-                "global_batch": a.batch_size * rt.world_size, "seq_len": a.seq_len,
-                "parallelism": f"ep{rt.world_size}+fsdp{rt.world_size}" if rt.world_size > 1 else "single-gpu",
+                "global_batch": a.batch_size * rt.world_size // self.cp, "seq_len": a.seq_len,
+                "parallelism": ((f"cp{self.cp}+" if self.cp > 1 else "") + f"ep{rt.world_size}+fsdp{rt.world_size}"
+                                if rt.world_size > 1 else "single-gpu"),
                 "optimizer": f"AdamW in-backward, fp32 master, {a.moment_dtype} moments",
                 "grad_ckpt": True, "l2": "256 MB buffer written between timed steps",
                 "loss_tokens": "last 50%",

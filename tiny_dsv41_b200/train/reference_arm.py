@@ -52,11 +52,13 @@ def run_reference_arm(args, metric: str, model_name: str):
     runtime = initialize_runtime(require_distributed=True)
     world = runtime.world_size
     try:
-        meshes = ParallelMeshes.build(cp=1, ep=world, device_type="cuda")
+        cp_size = getattr(args, "cp", 1)
+        meshes = ParallelMeshes.build(cp=cp_size, ep=world, device_type="cuda")
         dispatcher = AllToAllTokenDispatcher(meshes.ep) if meshes.ep is not None else TokenDispatcher()
         config = Qwen3MoeConfig(num_hidden_layers=args.layers, max_window_layers=args.layers)
+        cp = ContextParallel(meshes.cp)
         with torch.device("meta"):
-            model = Qwen3MoeForCausalLM(config, ContextParallel(None), dispatcher)
+            model = Qwen3MoeForCausalLM(config, cp, dispatcher)
         # bf16 storage from the start, as the stock loader (load_qwen3_moe with dtype=bf16) assigns it
         model = model.to(torch.bfloat16).to_empty(device=runtime.device)
         gen = torch.Generator(device="cuda")
@@ -72,9 +74,9 @@ def run_reference_arm(args, metric: str, model_name: str):
         apply_fsdp2(model, meshes)
         parameters = ParallelParameters.collect(model)
         optimizer = torch.optim.AdamW(model.parameters(), lr=args.lr, foreach=False)
-        cp = ContextParallel(None)
 
-        host = torch.Generator().manual_seed(1234 + runtime.rank)
+        # the ranks of one CP group train on the same sequences (the model keeps each rank's chunk)
+        host = torch.Generator().manual_seed(1234 + runtime.rank // cp_size)
         batches = []
         for _ in range(4):
             ids = torch.randint(0, config.vocab_size, (args.batch_size, args.seq_len), generator=host)
@@ -117,15 +119,17 @@ def run_reference_arm(args, metric: str, model_name: str):
         times = torch.tensor([device_ms, wall_ms], device=runtime.device)
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
         device_ms, wall_ms = times.tolist()
-        tokens = args.batch_size * args.seq_len * world * args.steps
+        tokens = args.batch_size * args.seq_len * (world // cp_size) * args.steps
         record = {
             "metric": metric, "impl": "reference", "value": tokens / (device_ms / 1000), "unit": "tokens/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": device_ms / args.steps,
             "higher_is_better": True, "scaling": "weak", "dtype": "bf16", "data": "synthetic", "vs_baseline": None,
             "e2e": {"value": tokens / (wall_ms / 1000), "unit": "tokens/s",
                     "h2d_bytes_per_step": 2 * args.batch_size * args.seq_len * 8, "d2h_bytes_per_step": 4},
-            "config": {"model": model_name, "global_batch": args.batch_size * world, "seq_len": args.seq_len,
-                       "parallelism": f"ep{world}+fsdp{world}", "optimizer": "torch AdamW on bf16 params (stock)",
+            "config": {"model": model_name, "global_batch": args.batch_size * world // cp_size,
+                       "seq_len": args.seq_len,
+                       "parallelism": (f"cp{cp_size}+" if cp_size > 1 else "") + f"ep{world}+fsdp{world // cp_size}",
+                       "optimizer": "torch AdamW on bf16 params (stock)",
                        "grad_ckpt": True, "l2": "256 MB buffer written between timed steps"},
         }
     except torch.OutOfMemoryError as error:
