@@ -73,8 +73,8 @@ enum : int {
 // Where the keys and values are. Keys are numbered globally; key tile j (128 keys) belongs to
 // owner j * 128 / chunk and starts at row b * chunk + (j * 128 mod chunk) of that owner's
 // [B, chunk, Hkv, 128] tensors. One owner holding the whole sequence (chunk = L, q_offset = 0)
-// is plain causal attention; under context parallelism owner c is CP rank c, whose tensors are
-// reached through its peer mapping, and this rank's queries start at global position q_offset.
+// is plain causal attention; under context parallelism owner c is CP rank c (its chunk copied into
+// this rank's memory beforehand), and this rank's queries start at global position q_offset.
 constexpr int kMaxOwners = 8;
 struct KvMaps {
   CUtensorMap k[kMaxOwners];
@@ -163,8 +163,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
       tma_load_3d(sm.q + kAtom, &tq, &sm.q_full, 64, h, row0);
       // K_j's slot frees when S_{j-2} completes, V_j's when PV_{j-2} does: separate barriers let the
       // next K tile load while the softmax of the current one still holds V. Key tile j lives in
-      // the chunk of its owner (another rank's memory under context parallelism: a plain TMA load
-      // over NVLink, never a multicast one).
+      // the chunk of its owner.
       for (int j = 0; j < n_kv; ++j) {
         const int s = j & 1;
         const int owner = kv.owner(j);
@@ -863,8 +862,8 @@ std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const
 
 // Context-parallel forward: this rank's queries q [B, Lq, H, 128] start at global position q_offset;
 // keys / values are split into chunks of `chunk` positions, chunk c at k_ptrs[c] / v_ptrs[c]
-// ([B, chunk, Hkv, 128] bf16; another rank's memory reached through its peer mapping). Tiles of
-// other ranks are read by plain (non-multicast) TMA loads straight into the softmax pipeline.
+// ([B, chunk, Hkv, 128] bf16 in this rank's memory: its own chunk, and the other ranks' chunks as
+// copied by attn_cp_pull).
 std::vector<at::Tensor> attn_fwd_cp(const at::Tensor& q, const std::vector<int64_t>& k_ptrs,
                                     const std::vector<int64_t>& v_ptrs, int64_t chunk, int64_t q_offset,
                                     int64_t kv_heads) {
@@ -1026,6 +1025,38 @@ at::Tensor attn_bwd_cp(const at::Tensor& dout, const at::Tensor& q, const std::v
              dq_acc + n_q + n_stat, nullptr);
   convert_to_bf16(dq_acc, dq, nullptr, nullptr, 1.f / sqrtf(static_cast<float>(kDim)));
   return dq;
+}
+
+namespace {
+// dst[c] <- src[c] for the first `n` chunks of `bytes` each (16-byte vectors; src are other ranks'
+// buffers reached through peer mappings and read with plain L2-cached loads, never by TMA).
+__global__ void cp_pull_kernel(const int64_t* __restrict__ src, int n, uint8_t* __restrict__ dst, int64_t vec) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int c = 0; c < n; ++c) {
+    const uint4* from = reinterpret_cast<const uint4*>(src[c]);
+    uint4* to = reinterpret_cast<uint4*>(dst) + static_cast<int64_t>(c) * vec;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < vec; i += stride)
+      to[i] = __ldcg(from + i);
+  }
+}
+}  // namespace
+
+// Copy the first `src.numel()` chunks (int64 device table of addresses, each `chunk_bytes` long)
+// into consecutive slots of `dst` (this rank's memory).
+void attn_cp_pull(const at::Tensor& src, at::Tensor& dst, int64_t chunk_bytes) {
+  check_cuda_tensor(src, "pull address table");
+  check_cuda_tensor(dst, "pull destination");
+  TDSV_CHECK(src.scalar_type() == at::kLong && src.dim() == 1, "pull address table: int64 [n]");
+  const int64_t n = src.numel();
+  TDSV_CHECK(chunk_bytes % 16 == 0 && dst.nbytes() >= static_cast<size_t>(n * chunk_bytes) &&
+                 reinterpret_cast<uintptr_t>(dst.data_ptr()) % 16 == 0,
+             "pull: 16-byte aligned chunks that fit the destination");
+  if (n == 0 || chunk_bytes == 0) return;
+  c10::cuda::CUDAGuard guard(dst.device());
+  const int64_t vec = chunk_bytes / 16;
+  cp_pull_kernel<<<static_cast<unsigned>(std::min<int64_t>((vec + 255) / 256, 148 * 4)), 256, 0, stream()>>>(
+      src.data_ptr<int64_t>(), static_cast<int>(n), reinterpret_cast<uint8_t*>(dst.data_ptr()), vec);
+  TDSV_LAUNCH_CHECK();
 }
 
 // This rank's (dk, dv) [B, chunk, Hkv, 128] bf16 from slot `me` of the outboxes of ranks me .. n - 1

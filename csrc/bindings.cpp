@@ -134,6 +134,7 @@ std::vector<at::Tensor> attn_fwd_cp(const at::Tensor& q, const std::vector<int64
 at::Tensor attn_bwd_cp(const at::Tensor& dout, const at::Tensor& q, const std::vector<int64_t>& k_ptrs,
                        const std::vector<int64_t>& v_ptrs, const at::Tensor& out, const at::Tensor& lse, int64_t chunk,
                        int64_t q_offset, int64_t kv_heads, at::Tensor& outbox);
+void attn_cp_pull(const at::Tensor& src, at::Tensor& dst, int64_t chunk_bytes);
 std::vector<at::Tensor> attn_cp_finalize(const at::Tensor& boxes, int64_t me, int64_t batch, int64_t chunk,
                                          int64_t kv_heads);
 }  // namespace tdsv
@@ -157,6 +158,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "context-parallel causal attention forward: keys / values read from each owner's chunk (peer memory)");
   m.def("attn_bwd_cp", &tdsv::attn_bwd_cp,
         "context-parallel attention backward: dq, with per-owner dK / dV partials in the local outbox");
+  m.def("attn_cp_pull", &tdsv::attn_cp_pull, "copy other ranks' K / V chunks into this rank's memory (peer loads)");
   m.def("attn_cp_finalize", &tdsv::attn_cp_finalize,
         "this rank's dk / dv: fixed-order sum of its slot in every rank's outbox (peer loads)");
   m.def("cache_fake_quant", &tdsv::cache_fake_quant, "FP8 / FP4 block fake quantization (0 fp8, 1 fp4_index, 2 fp4_kv)");

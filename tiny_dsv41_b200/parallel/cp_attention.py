@@ -1,28 +1,34 @@
-"""Context-parallel causal attention with the K/V exchange fused into the attention kernels
-(fused path 3).
+"""Context-parallel causal attention with the K/V exchange over NVLink peer memory instead of
+an all-gather (fused path 3).
 
 The reference gathers every rank's keys and values with an autograd all-gather and runs SDPA
 with an explicit [L_local, L] mask (``dsv41_train/cp.py:17-35``, ``dsv41_train/models/qwen/
-model.py:143-169``); the gather's backward is a reduce-scatter. Here nothing is gathered:
+model.py:143-169``); the gather's backward is a reduce-scatter. Here:
 
 * Each CP rank publishes its layer's K / V chunk into a symmetric buffer (one slot per layer,
   ``torch.distributed._symmetric_memory``), raises a ready flag and waits for its peers' flags.
-* The forward kernel (``attn_fwd_cp`` in ``csrc/attention.cu``) walks the visible key tiles in
-  global order and loads each tile by TMA straight from its owner's buffer - this rank's HBM or a
-  peer's over NVLink (plain loads, never a cluster-multicast load) - into the softmax pipeline.
-* The backward kernel (``attn_bwd_cp``) reads K / V the same way, keeps dQ local and reduce-adds
-  the dK / dV partials of every key owner into this rank's fp32 outbox (slot per owner). After a
-  flag exchange each owner sums its slot of every rank's outbox with peer loads in fixed rank
-  order (``attn_cp_finalize``): the reduce-scatter of the reference, done inside the attention
-  backward's epilogue kernel, deterministic.
+* Causal attention needs only the chunks of lower ranks. This rank copies exactly those into a
+  local staging buffer with its own peer-load kernel (``attn_cp_pull``: each remote byte crosses
+  NVLink once per use, instead of once per query tile), and the tcgen05 attention kernels
+  (``attn_fwd_cp`` / ``attn_bwd_cp`` in ``csrc/attention.cu``) walk the visible key tiles in
+  global order, each tile taken by TMA from the chunk of its owner in local memory.
+* The backward keeps dQ local and reduce-adds the dK / dV partials of every key owner into this
+  rank's fp32 outbox (one slot per owner). After a flag exchange each owner sums its slot of all
+  outboxes with peer loads in fixed rank order (``attn_cp_finalize``): the reduce-scatter of the
+  reference, done by the attention backward's epilogue kernel, deterministic.
+
+No kernel here issues a TMA load from another GPU's memory: an early version that streamed peer
+K / V tiles by TMA straight into the softmax pipeline produced wrong outputs for tiles of V read
+that way on B200 (the same bytes read with plain loads were correct), so remote data always lands
+in local memory first.
 
 Buffer reuse is guarded by epoch flags with bounded device waits (status 5 on timeout, raised by
 the training loop's status monitor): a rank rewrites its K / V slot of a layer only after every
 peer signalled that it finished reading the previous generation (after that layer's backward),
 and zeroes its outbox only after every owner finished summing the previous one.
 
-Activation checkpointing: the recompute of a layer (``parallel.replay`` mode ``replay``) reads the
-K / V already published by the first forward and exchanges nothing. A forward without autograd
+Activation checkpointing: the recompute of a layer (``parallel.replay`` mode ``replay``) re-pulls
+the K / V its first forward published and exchanges no flag. A forward without autograd
 (evaluation) releases its generation at once.
 
 Semantics: plain causal attention over the concatenation of the ranks' equal contiguous chunks
@@ -72,6 +78,11 @@ class CPAttentionWorkspace:
         slot = self.kv[0].numel() * 2  # bytes of one layer slot (K and V)
         self._slot_bytes = slot
         self._half_bytes = slot // 2
+        # local copies of the lower ranks' K / V chunks ([rank, 2, B, chunk, Hkv, 128]) and, per
+        # layer, the table of their slots in those ranks' memory
+        self.staging = torch.empty(max(self.rank, 1), 2, *shape, dtype=torch.bfloat16, device=device)
+        self._pull_tables = [torch.tensor([base + layer * slot for base in self._kv_bases[:self.rank]],
+                                          dtype=torch.int64, device=device) for layer in range(num_layers)]
         self.box_table = torch.tensor([int(p) for p in handles["outbox"].buffer_ptrs], dtype=torch.int64,
                                       device=device)
         self._flag_tables = [torch.tensor([int(p) + row * self.size * 4 for p in handles["flags"].buffer_ptrs],
@@ -96,9 +107,14 @@ class CPAttentionWorkspace:
             ops.ext().ep_wait(self.flags[row], epoch)
 
     # -- K / V slots ----------------------------------------------------------------------------
-    def kv_pointers(self, layer: int) -> tuple[list[int], list[int]]:
-        k = [base + layer * self._slot_bytes for base in self._kv_bases]
-        v = [p + self._half_bytes for p in k]
+    def pull(self, layer: int) -> tuple[list[int], list[int]]:
+        """Copy the lower ranks' K / V of `layer` into the staging buffer (peer loads); returns the
+        local K and V addresses of every visible owner's chunk (owners 0 .. rank)."""
+        if self.rank:
+            ops.ext().attn_cp_pull(self._pull_tables[layer], self.staging, self._slot_bytes)
+        staged = self.staging.data_ptr()
+        k = [staged + c * self._slot_bytes for c in range(self.rank)] + [self.kv[layer, 0].data_ptr()]
+        v = [p + self._half_bytes for p in k[:-1]] + [self.kv[layer, 1].data_ptr()]
         return k, v
 
     def publish(self, layer: int, k: torch.Tensor, v: torch.Tensor) -> None:
@@ -139,7 +155,7 @@ class _CPAttention(torch.autograd.Function):
         _, mode = replay.current()
         if mode != "replay":  # a recompute reads the generation its first forward published
             ws.publish(layer, k, v)
-        kp, vp = ws.kv_pointers(layer)
+        kp, vp = ws.pull(layer)
         out, lse = ops.ext().attn_fwd_cp(q, kp, vp, ws.chunk, ws.rank * ws.chunk, ws.kv_heads)
         if not torch.is_grad_enabled() and mode is None:
             ws.release(layer)  # no backward follows
@@ -151,11 +167,11 @@ class _CPAttention(torch.autograd.Function):
     def backward(ctx, dout):
         ws, layer = ctx.ws, ctx.layer
         q, out, lse = ctx.saved_tensors
-        kp, vp = ws.kv_pointers(layer)
+        kp, vp = ws.pull(layer)
+        ws.release(layer)  # the peers' K / V of this generation are no longer read
         ws.outbox_acquire()
         dq = ops.ext().attn_bwd_cp(dout.contiguous(), q, kp, vp, out, lse, ws.chunk, ws.rank * ws.chunk, ws.kv_heads,
                                    ws.outbox)
-        ws.release(layer)
         dk, dv = ws.outbox_exchange()
         return dq, dk, dv, None, None
 
