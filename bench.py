@@ -145,8 +145,16 @@ def run_native(args) -> None:
             emit({**base, "value": None, "unavailable": f"full config does not fit: {why}", "vs_baseline": None,
                   "config": {"model": MODEL, "seq_len": args.seq_len, "global_batch": args.batch_size * world}})
         return
-    bench = QwenSFTBench(args)
-    result = bench.run()
+    try:
+        bench = QwenSFTBench(args)
+        result = bench.run()
+    except torch.OutOfMemoryError as error:
+        # every rank reaches here or fails its next collective within the process-group timeout
+        if rank == 0:
+            emit({**base, "value": None, "vs_baseline": None,
+                  "unavailable": f"out of GPU memory at N={world}: {str(error).splitlines()[0][:200]}",
+                  "config": {"model": MODEL, "seq_len": args.seq_len, "cp": args.cp}})
+        return
     if rank == 0:
         record = {**base, **result}
         record["vs_baseline"] = (None if BASELINE_VALUE is None or record.get("value") is None
