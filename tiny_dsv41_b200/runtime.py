@@ -1,7 +1,8 @@
-"""Process/device bootstrap: one process per GPU, NCCL process group from the torchrun env.
+"""Process and device bootstrap: one process per GPU, the NCCL process group from the torchrun
+environment (gloo for CPU runs with WORLD_SIZE > 1, as the multi-rank tests use).
 
-API of ``dsv41_train/runtime.py:12-82`` (Runtime, initialize_runtime, local_tensor,
-distributed_mean). CPU runs (tests) use gloo when WORLD_SIZE > 1.
+Public names follow ``dsv41_train/runtime.py:12-82`` (``Runtime``, ``initialize_runtime``,
+``local_tensor``, ``distributed_mean``) so entry points written against either load the same way.
 """
 
 from __future__ import annotations
@@ -36,6 +37,24 @@ def choose_device(name: str) -> torch.device:
     return torch.device(name)
 
 
+def _env_defaults() -> None:
+    """A single process started without torchrun still gets a (world of one) process group."""
+    for key, value in (("MASTER_ADDR", "127.0.0.1"), ("MASTER_PORT", "29512"), ("RANK", "0"), ("WORLD_SIZE", "1")):
+        os.environ.setdefault(key, value)
+
+
+def _open_group(backend: str, timeout: datetime.timedelta | None, device: torch.device | None) -> None:
+    if dist.is_initialized():
+        return
+    _env_defaults()
+    options = {"backend": backend}
+    if timeout is not None:
+        options["timeout"] = timeout
+    if device is not None:
+        options["device_id"] = device
+    dist.init_process_group(**options)
+
+
 def initialize_runtime(
     device_name: str = "auto",
     local_rank_arg: int | None = None,
@@ -43,45 +62,27 @@ def initialize_runtime(
     require_distributed: bool = False,
     timeout_seconds: float | None = None,
 ) -> Runtime:
-    """Bind the torchrun worker to its local GPU and create the process group.
-
-    Single-process runs do not create a group unless ``require_distributed`` is set (a world of
-    one still gets a group then, so collective code paths stay uniform).
-    """
+    """Bind this torchrun worker to its local GPU and open the process group (NCCL on GPUs, gloo
+    on CPU runs). A single process opens no group unless ``require_distributed`` is set; then it
+    opens a world of one, so collective code paths stay the same."""
     world_size = int(os.environ.get("WORLD_SIZE", "1"))
     if world_size < 1:
         raise ValueError("WORLD_SIZE must be positive")
     if world_size == 1 and not require_distributed:
         return Runtime(device=choose_device(device_name))
     timeout = datetime.timedelta(seconds=timeout_seconds) if timeout_seconds else None
-    use_cuda = torch.cuda.is_available() and device_name in {"auto", "cuda"}
-    if not use_cuda:
-        if not dist.is_initialized():
-            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-            os.environ.setdefault("MASTER_PORT", "29512")
-            os.environ.setdefault("RANK", "0")
-            os.environ.setdefault("WORLD_SIZE", "1")
-            kwargs = {"backend": "gloo"}
-            if timeout:
-                kwargs["timeout"] = timeout
-            dist.init_process_group(**kwargs)
+    if not (torch.cuda.is_available() and device_name in ("auto", "cuda")):
+        _open_group("gloo", timeout, None)
         return Runtime(torch.device("cpu"), dist.get_rank(), int(os.environ.get("LOCAL_RANK", "0")),
                        dist.get_world_size())
-    local_rank_value = os.environ.get("LOCAL_RANK")
-    local_rank = int(local_rank_value) if local_rank_value is not None else (local_rank_arg or 0)
+    env_rank = os.environ.get("LOCAL_RANK")
+    local_rank = int(env_rank) if env_rank is not None else (local_rank_arg or 0)
     if not 0 <= local_rank < torch.cuda.device_count():
         raise RuntimeError(f"LOCAL_RANK {local_rank} is outside the {torch.cuda.device_count()} visible devices")
-    torch.cuda.set_device(local_rank)
-    if not dist.is_initialized():
-        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        os.environ.setdefault("MASTER_PORT", "29512")
-        os.environ.setdefault("RANK", "0")
-        os.environ.setdefault("WORLD_SIZE", "1")
-        kwargs = {"backend": "nccl", "device_id": torch.device("cuda", local_rank)}
-        if timeout:
-            kwargs["timeout"] = timeout
-        dist.init_process_group(**kwargs)
-    return Runtime(torch.device("cuda", local_rank), dist.get_rank(), local_rank, dist.get_world_size())
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    _open_group("nccl", timeout, device)
+    return Runtime(device, dist.get_rank(), local_rank, dist.get_world_size())
 
 
 def local_tensor(tensor: torch.Tensor) -> torch.Tensor:
@@ -89,12 +90,12 @@ def local_tensor(tensor: torch.Tensor) -> torch.Tensor:
 
 
 def distributed_mean(value: torch.Tensor, runtime: Runtime) -> float:
-    value = value.detach().float()
+    """Mean of a scalar over all ranks (the value itself on a single process)."""
+    total = value.detach().float().clone()
     if runtime.distributed and dist.is_initialized():
-        value = value.clone()
-        dist.all_reduce(value, op=dist.ReduceOp.SUM)
-        value /= runtime.world_size
-    return value.item()
+        dist.all_reduce(total, op=dist.ReduceOp.SUM)
+        return total.item() / runtime.world_size
+    return total.item()
 
 
 __all__ = ["Runtime", "choose_device", "distributed_mean", "initialize_runtime", "local_tensor"]
