@@ -14,7 +14,7 @@ import random
 from pathlib import Path
 
 from .data import PromptRecord, build_reward
-from .rewards import _numeric_answer
+from .rewards import parse_number
 
 DATASET_REVISION = "3101c7d5072418e28b9008a6636bde82a006892c"
 SPLIT_SHA256 = {"train": "17f347dc51477c50d4efb83959dbb7c56297aba886e5544ee2aaed3024813465",
@@ -34,7 +34,7 @@ def load_split(path, split: str):
                 or not isinstance(row.get("answer"), str) or "####" not in row["answer"]):
             raise ValueError(f"{path}:{index + 1}: not an official GSM8K question/answer record")
         answer = row["answer"].rsplit("####", 1)[1].strip()
-        _numeric_answer(answer)  # a malformed reference answer aborts instead of scoring zero
+        parse_number(answer)  # a malformed reference answer aborts instead of scoring zero
         rows.append({"id": f"gsm8k:{split}:{index}", "question": row["question"], "answer": answer})
     if len(rows) != SPLIT_SIZE[split] or len({r["question"] for r in rows}) != len(rows):
         raise ValueError(f"official GSM8K {split} must contain {SPLIT_SIZE[split]} distinct questions")
@@ -96,7 +96,7 @@ def formatting_correct(text: str) -> bool:
     if "####" not in text:
         return False
     try:
-        _numeric_answer(text.rsplit("####", 1)[1].strip())
+        parse_number(text.rsplit("####", 1)[1].strip())
         return True
     except (ValueError, ArithmeticError):
         return False

@@ -1,10 +1,12 @@
-"""Checkpoint tokenization without executing tokenizer code from the checkpoint.
+"""Tokenization of a checkpoint directory without running any code the checkpoint ships.
 
-Same public API as ``dsv41_train/rl/tokenizer.py`` (``ModelTokenizer.encode_prompt``,
+Public API of ``dsv41_train/rl/tokenizer.py`` (``ModelTokenizer.encode_prompt``,
 ``encode_conversation``, ``encode_completion``, ``decode``, ``eos_token_ids``,
-``read_eos_token_ids``): ``tokenizer.json`` through the ``tokenizers`` library and the
-checkpoint's chat template rendered by a sandboxed jinja2 environment, then tokenized without
-added special tokens (what HF ``apply_chat_template`` does).
+``read_eos_token_ids``). ``tokenizer.json`` is read by the ``tokenizers`` library; the chat
+template (``chat_template.jinja``, or ``chat_template`` in tokenizer_config.json, possibly a list
+of named templates with a ``default``) is rendered in a sandboxed, immutable jinja2 environment
+and the rendered text is tokenized without added special tokens - what HF
+``apply_chat_template`` does.
 """
 
 from __future__ import annotations
@@ -16,8 +18,12 @@ from jinja2 import TemplateError
 from jinja2.sandbox import ImmutableSandboxedEnvironment
 from tokenizers import Tokenizer
 
+_SPECIAL = ("bos_token", "eos_token", "pad_token", "unk_token")
+_ROLES = ("system", "user", "assistant")
 
-def _read_json(directory: Path, name: str) -> dict:
+
+def _json_object(directory: Path, name: str) -> dict:
+    """The JSON object in ``directory/name``, or {} when the file does not exist."""
     path = directory / name
     if not path.exists():
         return {}
@@ -30,92 +36,95 @@ def _read_json(directory: Path, name: str) -> dict:
     return value
 
 
-def _token_ids(value, name: str) -> tuple[int, ...]:
-    values = value if isinstance(value, (list, tuple)) else [value]
-    if not values or any(type(v) is not int or v < 0 for v in values):
+def _nested(config: dict) -> dict:
+    text = config.get("text_config", {})
+    return text if isinstance(text, dict) else {}
+
+
+def _id_tuple(value, name: str) -> tuple[int, ...]:
+    items = list(value) if isinstance(value, (list, tuple)) else [value]
+    if not items or not all(type(i) is int and i >= 0 for i in items):
         raise ValueError(f"{name} must be a nonnegative integer or a nonempty list of them")
-    return tuple(dict.fromkeys(values))
+    return tuple(dict.fromkeys(items))  # distinct, first occurrence order
 
 
 def read_eos_token_ids(model_dir, fallback=None) -> tuple[int, ...]:
-    """Stop ids from generation_config.json, config.json or its text_config (first present)."""
+    """Stop ids from the first of generation_config.json, config.json and its text_config that
+    names them; else ``fallback`` (or none)."""
     directory = Path(model_dir)
-    config = _read_json(directory, "config.json")
-    text = config.get("text_config", {}) if isinstance(config.get("text_config", {}), dict) else {}
-    for source in (_read_json(directory, "generation_config.json"), config, text):
+    config = _json_object(directory, "config.json")
+    for source in (_json_object(directory, "generation_config.json"), config, _nested(config)):
         if source.get("eos_token_id") is not None:
-            return _token_ids(source["eos_token_id"], "eos_token_id")
-    return () if fallback is None else _token_ids(fallback, "eos_token_id")
+            return _id_tuple(source["eos_token_id"], "eos_token_id")
+    return () if fallback is None else _id_tuple(fallback, "eos_token_id")
 
 
-def _chat_template(directory: Path, config: dict) -> str | None:
-    path = directory / "chat_template.jinja"
-    template = path.read_text(encoding="utf-8") if path.exists() else config.get("chat_template")
+def _template_source(directory: Path, tokenizer_config: dict) -> str | None:
+    file = directory / "chat_template.jinja"
+    template = file.read_text(encoding="utf-8") if file.exists() else tokenizer_config.get("chat_template")
     if template is None:
         return None
-    if isinstance(template, list):
-        choices = {}
+    if isinstance(template, list):  # named templates
+        named = {}
         for entry in template:
-            if not isinstance(entry, dict) or not isinstance(entry.get("name"), str) or entry["name"] in choices:
+            name = entry.get("name") if isinstance(entry, dict) else None
+            if not isinstance(name, str) or name in named:
                 raise ValueError("chat template list must contain unique named templates")
-            choices[entry["name"]] = entry["template"]
-        template = choices
+            named[name] = entry["template"]
+        template = named
     if isinstance(template, dict):
         if "default" not in template:
             raise ValueError("named chat templates require a 'default' template")
         template = template["default"]
-    if not isinstance(template, str) or not template.strip():
+    if not (isinstance(template, str) and template.strip()):
         raise ValueError("chat template must be a nonempty string")
     return template
 
 
-def _token_text(value):
-    if isinstance(value, dict):
-        return value.get("content")
-    return value
+def _raise_from_template(message):
+    raise TemplateError(message)
 
 
 class ModelTokenizer:
     def __init__(self, model_dir):
         directory = Path(model_dir)
-        path = directory / "tokenizer.json"
-        if not path.is_file():
-            raise ValueError(f"{path} is required; only local tokenizers tokenizer.json checkpoints are supported")
+        vocab_file = directory / "tokenizer.json"
+        if not vocab_file.is_file():
+            raise ValueError(f"{vocab_file} is required; only local tokenizers tokenizer.json checkpoints are supported")
         try:
-            self._tokenizer = Tokenizer.from_file(str(path))
+            self._tokenizer = Tokenizer.from_file(str(vocab_file))
         except Exception as error:
-            raise ValueError(f"unsupported or invalid tokenizer.json at {path}: {error}") from error
-        vocabulary = self._tokenizer.get_vocab(with_added_tokens=True)
-        self._vocabulary_ids = set(vocabulary.values())
-        config = _read_json(directory, "config.json")
-        text_config = config.get("text_config", {}) if isinstance(config.get("text_config", {}), dict) else {}
-        tok_config = _read_json(directory, "tokenizer_config.json")
-        self._template_source = _chat_template(directory, tok_config)
-        vocab_size = config.get("vocab_size", text_config.get("vocab_size"))
-        if vocab_size is not None and any(i >= vocab_size for i in vocabulary.values()):
+            raise ValueError(f"unsupported or invalid tokenizer.json at {vocab_file}: {error}") from error
+        known = set(self._tokenizer.get_vocab(with_added_tokens=True).values())
+        self._known_ids = known
+        config = _json_object(directory, "config.json")
+        tokenizer_config = _json_object(directory, "tokenizer_config.json")
+        model_vocab = config.get("vocab_size", _nested(config).get("vocab_size"))
+        if model_vocab is not None and max(known, default=-1) >= model_vocab:
             raise ValueError("tokenizer vocabulary contains IDs outside the model vocabulary")
-        self.special = {}
-        for name in ("bos_token", "eos_token", "pad_token", "unk_token"):
-            text = _token_text(tok_config.get(name))
-            if text is None:
-                value = tok_config.get(name + "_id", config.get(name + "_id", text_config.get(name + "_id")))
-                if value is not None:
-                    text = self._tokenizer.id_to_token(_token_ids(value, name)[0])
-            self.special[name] = text
-        fallback = None
-        if self.special["eos_token"] is not None:
-            fallback = self._tokenizer.token_to_id(self.special["eos_token"])
+        self.special = {name: self._special_text(name, tokenizer_config, config) for name in _SPECIAL}
+        eos_text = self.special["eos_token"]
+        fallback = None if eos_text is None else self._tokenizer.token_to_id(eos_text)
         self._eos_token_ids = read_eos_token_ids(directory, fallback=fallback)
         for token_id in self._eos_token_ids:
-            self._validate_id(token_id, "eos_token_id")
-        self.add_bos = bool(tok_config.get("add_bos_token", False))
-        self._env = ImmutableSandboxedEnvironment(trim_blocks=True, lstrip_blocks=True)
+            self._check_id(token_id, "eos_token_id")
+        self.add_bos = bool(tokenizer_config.get("add_bos_token", False))
+        source = _template_source(directory, tokenizer_config)
+        environment = ImmutableSandboxedEnvironment(trim_blocks=True, lstrip_blocks=True)
+        environment.globals["raise_exception"] = _raise_from_template
+        self._template_source = source
+        self._template = environment.from_string(source) if source else None
 
-        def raise_exception(message):
-            raise TemplateError(message)
-
-        self._env.globals["raise_exception"] = raise_exception
-        self._template = self._env.from_string(self._template_source) if self._template_source else None
+    def _special_text(self, name: str, tokenizer_config: dict, config: dict):
+        value = tokenizer_config.get(name)
+        text = value.get("content") if isinstance(value, dict) else value
+        if text is not None:
+            return text
+        key = name + "_id"
+        owner = next((source for source in (tokenizer_config, config, _nested(config)) if key in source), None)
+        if owner is None or owner[key] is None:
+            return None
+        return self._tokenizer.id_to_token(_id_tuple(owner[key], name)[0])
 
     @property
     def eos_token_ids(self) -> tuple[int, ...]:
@@ -126,68 +135,19 @@ class ModelTokenizer:
         text = self.special.get("pad_token")
         return None if text is None else self._tokenizer.token_to_id(text)
 
-    def _validate_id(self, token_id, name):
-        if type(token_id) is not int or token_id not in self._vocabulary_ids:
-            raise ValueError(f"{name} contains an ID outside the tokenizer vocabulary: {token_id!r}")
+    def _check_id(self, token_id, what: str) -> None:
+        if type(token_id) is not int or token_id not in self._known_ids:
+            raise ValueError(f"{what} contains an ID outside the tokenizer vocabulary: {token_id!r}")
 
+    # -- encoding -------------------------------------------------------------------------------
     def encode_text(self, text: str, *, add_special_tokens: bool = False) -> list[int]:
         return self._tokenizer.encode(text, add_special_tokens=add_special_tokens).ids
 
-    def encode_prompt(self, prompt: str | None = None, messages: list[dict] | None = None) -> list[int]:
-        if (prompt is None) == (messages is None):
-            raise ValueError("provide exactly one of prompt or messages")
-        if prompt is not None:
-            if not isinstance(prompt, str) or not prompt.strip():
-                raise ValueError("prompt must be a nonempty string")
-            if self._template is None:
-                return self.encode_text(prompt, add_special_tokens=True)
-            messages = [{"role": "user", "content": prompt}]
-        if self._template is None:
-            raise ValueError("messages require a checkpoint chat template")
-        self._check_messages(messages, final_user=True)
-        return self._encode_template(messages)
-
-    def encode_conversation(self, messages, *, tools=None, chat_template_kwargs=None) -> list[int]:
-        if self._template is None:
-            raise ValueError("conversations require a checkpoint chat template")
-        options = dict(chat_template_kwargs or {})
-        if set(options) - {"enable_thinking"}:
-            raise ValueError("chat_template_kwargs support only enable_thinking")
-        if not isinstance(messages, list) or not messages:
-            raise ValueError("messages must be a nonempty list")
-        if messages[-1].get("role") not in ("user", "tool"):
-            raise ValueError("conversations must end with a user message or completed tool results")
-        return self._encode_template(messages, tools=tools, **options)
-
-    def encode_completion(self, messages, answer: str, *, chat_template_kwargs=None) -> tuple[list[int], list[int]]:
-        """(generation prompt ids, completed conversation ids); the prompt must be a token prefix."""
-        if not isinstance(answer, str) or not answer.strip():
-            raise ValueError("answer must be a nonempty string")
-        prompt_ids = self.encode_conversation(messages, chat_template_kwargs=chat_template_kwargs)
-        full_ids = self._encode_template([*messages, {"role": "assistant", "content": answer}],
-                                         add_generation_prompt=False, **(chat_template_kwargs or {}))
-        if full_ids[:len(prompt_ids)] != prompt_ids:
-            raise ValueError("completed conversation does not preserve the generation prompt token prefix")
-        return prompt_ids, full_ids
-
-    def _check_messages(self, messages, *, final_user: bool):
-        if not isinstance(messages, list) or not messages:
-            raise ValueError("messages must be a nonempty list")
-        for m in messages:
-            if not isinstance(m, dict) or set(m) != {"role", "content"}:
-                raise ValueError("messages support only role and content")
-            if m["role"] not in ("system", "user", "assistant"):
-                raise ValueError("message role must be system, user, or assistant")
-            if not isinstance(m["content"], str) or not m["content"].strip():
-                raise ValueError("message content must be nonempty text")
-        if final_user and messages[-1]["role"] != "user":
-            raise ValueError("messages must end with a user message for generation")
-
-    def _encode_template(self, messages, *, add_generation_prompt=True, tools=None, **kwargs):
+    def _render(self, messages, *, add_generation_prompt=True, tools=None, **options) -> list[int]:
+        variables = {name: text for name, text in self.special.items() if text is not None}
         try:
-            text = self._template.render(messages=messages, add_generation_prompt=add_generation_prompt,
-                                         tools=tools, **{k: v for k, v in self.special.items() if v is not None},
-                                         **kwargs)
+            text = self._template.render(messages=messages, add_generation_prompt=add_generation_prompt, tools=tools,
+                                         **variables, **options)
         except (TemplateError, TypeError, ValueError) as error:
             raise ValueError(f"cannot render checkpoint chat template: {error}") from error
         ids = self.encode_text(text)
@@ -195,10 +155,64 @@ class ModelTokenizer:
             raise ValueError("chat template must produce a nonempty list of token IDs")
         return ids
 
+    @staticmethod
+    def _plain_messages(messages) -> None:
+        if not isinstance(messages, list) or not messages:
+            raise ValueError("messages must be a nonempty list")
+        for message in messages:
+            if not isinstance(message, dict) or set(message) != {"role", "content"}:
+                raise ValueError("messages support only role and content")
+            if message["role"] not in _ROLES:
+                raise ValueError("message role must be system, user, or assistant")
+            if not (isinstance(message["content"], str) and message["content"].strip()):
+                raise ValueError("message content must be nonempty text")
+        if messages[-1]["role"] != "user":
+            raise ValueError("messages must end with a user message for generation")
+
+    def encode_prompt(self, prompt: str | None = None, messages: list[dict] | None = None) -> list[int]:
+        """Generation prompt ids for one prompt text or a chat; plain text without a template is
+        tokenized with the tokenizer's own special tokens."""
+        if (prompt is None) == (messages is None):
+            raise ValueError("provide exactly one of prompt or messages")
+        if prompt is not None:
+            if not (isinstance(prompt, str) and prompt.strip()):
+                raise ValueError("prompt must be a nonempty string")
+            if self._template is None:
+                return self.encode_text(prompt, add_special_tokens=True)
+            messages = [{"role": "user", "content": prompt}]
+        elif self._template is None:
+            raise ValueError("messages require a checkpoint chat template")
+        self._plain_messages(messages)
+        return self._render(messages)
+
+    def encode_conversation(self, messages, *, tools=None, chat_template_kwargs=None) -> list[int]:
+        if self._template is None:
+            raise ValueError("conversations require a checkpoint chat template")
+        options = dict(chat_template_kwargs or {})
+        if not set(options) <= {"enable_thinking"}:
+            raise ValueError("chat_template_kwargs support only enable_thinking")
+        if not (isinstance(messages, list) and messages):
+            raise ValueError("messages must be a nonempty list")
+        if messages[-1].get("role") not in ("user", "tool"):
+            raise ValueError("conversations must end with a user message or completed tool results")
+        return self._render(messages, tools=tools, **options)
+
+    def encode_completion(self, messages, answer: str, *, chat_template_kwargs=None) -> tuple[list[int], list[int]]:
+        """(generation prompt ids, ids of the conversation completed by ``answer``); the prompt must
+        be a token prefix of the completed conversation."""
+        if not (isinstance(answer, str) and answer.strip()):
+            raise ValueError("answer must be a nonempty string")
+        prompt = self.encode_conversation(messages, chat_template_kwargs=chat_template_kwargs)
+        completed = self._render([*messages, {"role": "assistant", "content": answer}], add_generation_prompt=False,
+                                 **(chat_template_kwargs or {}))
+        if completed[:len(prompt)] != prompt:
+            raise ValueError("completed conversation does not preserve the generation prompt token prefix")
+        return prompt, completed
+
     def decode(self, ids, *, skip_special_tokens=True) -> str:
         ids = list(ids)
-        for i in ids:
-            self._validate_id(i, "decoded token IDs")
+        for token_id in ids:
+            self._check_id(token_id, "decoded token IDs")
         return self._tokenizer.decode(ids, skip_special_tokens=skip_special_tokens)
 
 
