@@ -58,6 +58,39 @@ class _ScaleGradient(torch.autograd.Function):
         return grad * ctx.scale, None
 
 
+@dataclass
+class _RowRoute:
+    """Where the looked-up ids of one rank go: ``order`` groups the flat ids by owning rank
+    (stable), ``send[r]`` ids are asked of rank r and ``recv[r]`` ids are asked of this rank by r."""
+
+    order: torch.Tensor
+    send: list[int]
+    recv: list[int]
+    group: object
+
+    @classmethod
+    def plan(cls, owners: torch.Tensor, size: int, group) -> "_RowRoute":
+        asked = torch.bincount(owners, minlength=size)
+        asked_of_me = torch.empty_like(asked)
+        dist.all_to_all_single(asked_of_me, asked, group=group)
+        return cls(torch.argsort(owners, stable=True), asked.tolist(), asked_of_me.tolist(), group)
+
+    def requests_for_me(self, flat: torch.Tensor) -> torch.Tensor:
+        incoming = flat.new_empty(sum(self.recv))
+        dist.all_to_all_single(incoming, flat.index_select(0, self.order).contiguous(), output_split_sizes=self.recv,
+                               input_split_sizes=self.send, group=self.group)
+        return incoming
+
+    def rows_back(self, served: torch.Tensor) -> torch.Tensor:
+        import torch.distributed.nn.functional as dist_nn
+
+        grouped = served.new_empty((sum(self.send), served.shape[1]))
+        grouped = dist_nn.all_to_all_single(grouped, served.contiguous(), output_split_sizes=self.send,
+                                            input_split_sizes=self.recv, group=self.group)
+        # undo the grouping by owner: row k of `grouped` belongs at flat position order[k]
+        return grouped.new_zeros(grouped.shape).index_copy(0, self.order, grouped)
+
+
 class RowShardedEmbedding(nn.Module):
     """Embedding rows sharded over a mesh; lookups are routed to their owning rank and back.
 
@@ -101,24 +134,13 @@ class RowShardedEmbedding(nn.Module):
     def forward(self, indices: torch.Tensor) -> torch.Tensor:
         if self.size == 1:
             return self._lookup(indices)
-        import torch.distributed.nn.functional as dist_nn
-
-        shape = indices.shape
         flat = indices.reshape(-1)
-        owners = self.owners(flat)
-        order = torch.argsort(owners, stable=True)
-        send = torch.bincount(owners, minlength=self.size)
-        recv = torch.empty_like(send)
-        dist.all_to_all_single(recv, send, group=self.group)
-        send_splits, recv_splits = send.tolist(), recv.tolist()
-        requested = flat.new_empty(sum(recv_splits))
-        dist.all_to_all_single(requested, flat[order].contiguous(), output_split_sizes=recv_splits,
-                               input_split_sizes=send_splits, group=self.group)
-        rows = _ScaleGradient.apply(self._lookup(requested - self.row_start), 1.0 / self.size)
-        out = rows.new_empty((sum(send_splits), self.embedding_dim))
-        returned = dist_nn.all_to_all_single(out, rows.contiguous(), output_split_sizes=send_splits,
-                                             input_split_sizes=recv_splits, group=self.group)
-        return returned[torch.argsort(order)].view(*shape, self.embedding_dim)
+        route = _RowRoute.plan(self.owners(flat), self.size, self.group)
+        wanted = route.requests_for_me(flat)
+        # every owner's rows flow back to each requester; the gradient of a row that several ranks
+        # requested is summed over them, so it is scaled by 1 / mesh size as the reference does
+        served = _ScaleGradient.apply(self._lookup(wanted - self.row_start), 1.0 / self.size)
+        return route.rows_back(served).view(*indices.shape, self.embedding_dim)
 
     def _lookup(self, indices: torch.Tensor) -> torch.Tensor:
         if self._cpu_lookup is not None:
@@ -301,20 +323,25 @@ class DecoderLayer(nn.Module):
         self.attention_hc = HyperConnection(config)
         self.moe_hc = HyperConnection(config)
 
+    @staticmethod
+    def _branch(hc, streams, pre_mix, body):
+        """One hyper-connected branch: collapse the streams with ``pre_mix``, run ``body`` on the
+        collapsed row, expand its output back into the streams; returns the new streams, the
+        next branch's pre-mix weights and whatever else ``body`` returned."""
+        collapsed, next_pre, post, comb = hc(streams, pre_mix)
+        value, *extra = body(collapsed)
+        return hc.finish(value, streams, post, comb), next_pre, extra
+
     def forward(self, streams, pre_mix, context, shadow, engram_rows):
         if self.engram is not None:
             streams = self.engram(streams, engram_rows, context.token_mask)
-        residual = streams
         with nvtx_range("attention"):
-            collapsed, next_pre, post, comb = self.attention_hc(streams, pre_mix)
-            value = self.attention(self.input_norm(collapsed), context, shadow)
-            streams = self.attention_hc.finish(value, residual, post, comb)
-        residual = streams
+            streams, pre_mix, _ = self._branch(
+                self.attention_hc, streams, pre_mix, lambda x: (self.attention(self.input_norm(x), context, shadow),))
         with nvtx_range("moe"):
-            collapsed, final_pre, post, comb = self.moe_hc(streams, next_pre)
-            value, logits = self.moe(self.post_attention_norm(collapsed))
-            streams = self.moe_hc.finish(value, residual, post, comb)
-        return streams, final_pre, logits
+            streams, pre_mix, (logits,) = self._branch(self.moe_hc, streams, pre_mix,
+                                                       lambda x: self.moe(self.post_attention_norm(x)))
+        return streams, pre_mix, logits
 
 
 class DeepSeekV41Model(nn.Module):
@@ -341,58 +368,65 @@ class DeepSeekV41Model(nn.Module):
             for i in self.engram_layer_ids})
         self.gradient_checkpointing = False
 
-    def forward(self, input_ids, attention_mask=None, sequence_ids=None):
+    def _inputs(self, input_ids, attention_mask, sequence_ids):
+        """Validated (ids, live-token mask, sequence ids with padding set to -1) on the embedding's
+        device."""
         if input_ids.ndim != 2 or input_ids.shape[1] == 0:
             raise ValueError("input_ids must have shape [batch, nonempty sequence]")
         input_ids = input_ids.to(self.embedding.weight.device)
         if input_ids.shape[1] > self.config.max_position_embeddings:
             raise ValueError("sequence is longer than max_position_embeddings")
-        if attention_mask is None:
-            attention_mask = torch.ones_like(input_ids, dtype=torch.bool)
-        else:
-            if attention_mask.shape != input_ids.shape:
-                raise ValueError("attention_mask must match input_ids")
-            attention_mask = attention_mask.to(device=input_ids.device, dtype=torch.bool)
-        if sequence_ids is None:
-            sequence_ids = torch.zeros_like(input_ids)
-        elif sequence_ids.shape != input_ids.shape:
-            raise ValueError("sequence_ids must have the same shape as input_ids")
-        sequence_ids = sequence_ids.to(input_ids.device).masked_fill(~attention_mask, -1)
-        context = ModelContext.build(self.context_parallel, input_ids, attention_mask, sequence_ids,
-                                     self.config.sliding_window)
+        for name, given in (("attention_mask", attention_mask), ("sequence_ids", sequence_ids)):
+            if given is not None and given.shape != input_ids.shape:
+                raise ValueError("attention_mask must match input_ids" if name == "attention_mask"
+                                 else "sequence_ids must have the same shape as input_ids")
+        live = (torch.ones_like(input_ids, dtype=torch.bool) if attention_mask is None
+                else attention_mask.to(device=input_ids.device, dtype=torch.bool))
+        seq = torch.zeros_like(input_ids) if sequence_ids is None else sequence_ids.to(input_ids.device)
+        return input_ids, live, seq.masked_fill(~live, -1)
+
+    def _engram_rows(self, input_ids, live, sequence_ids) -> dict:
+        """Per Engram layer, the rows its n-gram hashes select (this CP rank's tokens)."""
+        if self.hash is None:
+            return {}
+        hashes = self.context_parallel.shard(self.hash(input_ids, live, sequence_ids))
+        return {layer: self.engram_tables[str(layer)](hashes[:, :, slot])
+                for slot, layer in enumerate(self.engram_layer_ids)}
+
+    def _context_on(self, contexts: dict, device):
+        if device not in contexts:  # layers placed on several devices each get a copy of the context
+            base = next(iter(contexts.values()))
+            contexts[device] = replace(base, **{f.name: getattr(base, f.name).to(device) for f in fields(base)
+                                                if isinstance(getattr(base, f.name), torch.Tensor)})
+        return contexts[device]
+
+    def forward(self, input_ids, attention_mask=None, sequence_ids=None):
+        input_ids, live, sequence_ids = self._inputs(input_ids, attention_mask, sequence_ids)
+        context = ModelContext.build(self.context_parallel, input_ids, live, sequence_ids, self.config.sliding_window)
         contexts = {input_ids.device: context}
-        hashes = self.hash(input_ids, attention_mask, sequence_ids) if self.hash is not None else None
+        engram_rows = self._engram_rows(input_ids, live, sequence_ids)
         hidden = self.embedding(context.input_ids)
-        batch, length = context.input_ids.shape
-        streams = hidden.unsqueeze(2).expand(-1, -1, self.config.hc_mult, -1).contiguous()
-        engram_rows: dict[int, torch.Tensor] = {}
-        if hashes is not None:
-            hashes = self.context_parallel.shard(hashes)
-            for index, layer in enumerate(self.engram_layer_ids):
-                engram_rows[layer] = self.engram_tables[str(layer)](hashes[:, :, index])
-        pre_mix = hidden.new_zeros(batch, length, self.config.hc_mult, dtype=torch.float32)
-        pre_mix[..., 0] = 1
-        empty = hidden.new_empty(0)
-        shadow = ShadowIndexers().dump(empty)
-        use_ckpt = self.gradient_checkpointing and self.training and torch.is_grad_enabled()
-        loader = partial(checkpoint, context_fn=replay.checkpoint_contexts) if use_ckpt else _direct
+        # hc_mult copies of the embedding; the first branch collapses them with weight 1 on stream 0
+        streams = hidden.unsqueeze(2).repeat(1, 1, self.config.hc_mult, 1)
+        pre_mix = torch.nn.functional.one_hot(torch.zeros(hidden.shape[:2], dtype=torch.long, device=hidden.device),
+                                              self.config.hc_mult).float()
+        none = hidden.new_empty(0)
+        shadow = ShadowIndexers().dump(none)
+        checkpointed = self.gradient_checkpointing and self.training and torch.is_grad_enabled()
+        run = partial(checkpoint, context_fn=replay.checkpoint_contexts) if checkpointed else _direct
         router_logits = []
         for layer in self.layers:
             device = next(layer.parameters()).device
-            if device not in contexts:
-                contexts[device] = replace(context, **{
-                    f.name: v.to(device) for f in fields(context)
-                    if isinstance(v := getattr(context, f.name), torch.Tensor)})
+            local = self._context_on(contexts, device)
             streams, pre_mix = streams.to(device), pre_mix.to(device)
-            shadow = tuple(v.to(device) for v in shadow)
-            streams, pre_mix, logits, *shadow = loader(
-                lambda *args, current=layer, local=contexts[device]: self._forward_layer(current, local, *args),
-                streams, pre_mix, engram_rows.get(layer.layer_id, empty).to(device), *shadow, use_reentrant=False)
+            step = lambda *args, current=layer, ctx=local: self._forward_layer(current, ctx, *args)  # noqa: E731
+            streams, pre_mix, logits, *shadow = run(step, streams, pre_mix,
+                                                    engram_rows.get(layer.layer_id, none).to(device),
+                                                    *(t.to(device) for t in shadow), use_reentrant=False)
             router_logits.append(logits)
         device = self.norm.weight.device
         with torch.cuda.device(device) if device.type == "cuda" else nullcontext():
-            hidden = HyperConnection.collapse(streams.to(device), pre_mix.to(device))
-            return self.norm(hidden), tuple(router_logits)
+            return self.norm(HyperConnection.collapse(streams.to(device), pre_mix.to(device))), tuple(router_logits)
 
     def _forward_layer(self, layer, context, streams, pre_mix, engram_row, *shadow_tensors):
         shadow = ShadowIndexers.load(shadow_tensors)
@@ -403,28 +437,25 @@ class DeepSeekV41Model(nn.Module):
 
 
 def load_balancing_loss(router_logits, num_experts: int, topk: int, attention_mask, context_parallel=None):
-    """E * sum_e (assignments_e / total) * (probabilities_e / total) over all layers' live tokens."""
+    """E * sum_e f_e * P_e over the live tokens of all layers: f_e is the fraction of top-k
+    assignments that go to expert e, P_e the mean router probability of e (softmax of the fp32
+    logits); under context parallelism both are totalled over the CP group first."""
     device = router_logits[0].device
-    assignments = torch.zeros(num_experts, device=device)
-    probabilities = torch.zeros(num_experts, device=device)
-    total = torch.zeros((), device=device)
-    mask = None if attention_mask is None else attention_mask.flatten().float().to(device)
-    for logits in router_logits:
-        probs = torch.softmax(logits.float().to(device), dim=-1)
-        selected = probs.topk(topk, dim=-1).indices
-        if mask is None:
-            assignments += torch.bincount(selected.flatten(), minlength=num_experts)
-            probabilities += probs.sum(0)
-            total += probs.shape[0]
-        else:
-            assignments.scatter_add_(0, selected.flatten(), mask.repeat_interleave(topk))
-            probabilities += (probs * mask.unsqueeze(-1)).sum(0)
-            total += mask.sum()
+    probs = torch.softmax(torch.cat([logits.float().to(device) for logits in router_logits]), dim=-1)
+    layers = len(router_logits)
+    if attention_mask is None:
+        weight = torch.ones(probs.shape[0], device=device)
+    else:
+        weight = attention_mask.flatten().float().to(device).repeat(layers)
+    chosen = probs.topk(topk, dim=-1).indices
+    counts = torch.zeros(num_experts, device=device).index_add(0, chosen.flatten(), weight.repeat_interleave(topk))
+    mass = (probs * weight.unsqueeze(-1)).sum(0)
+    tokens = weight.sum()
     if context_parallel is not None:
-        assignments = context_parallel.sum(assignments)
-        probabilities = context_parallel.sum(probabilities, autograd=True)
-        total = context_parallel.sum(total)
-    return num_experts * ((assignments / total) * (probabilities / total)).sum()
+        counts = context_parallel.sum(counts)
+        mass = context_parallel.sum(mass, autograd=True)
+        tokens = context_parallel.sum(tokens)
+    return num_experts * ((counts / tokens) * (mass / tokens)).sum()
 
 
 @dataclass
