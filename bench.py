@@ -22,7 +22,6 @@ import json
 import os
 import subprocess
 import sys
-import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -48,11 +47,20 @@ def parse_args(argv=None):
     p.add_argument("--moment-dtype", choices=("auto", "fp32", "bf16"), default="auto",
                    help="auto: fp32 AdamW moments when they fit in HBM at this N, else bf16")
     p.add_argument("--lr", type=float, default=1e-5)
+    p.add_argument("--dense-sync", choices=("auto", "peer", "fsdp"), default="auto",
+                   help="dense weights: peer = bf16 replicas + sharded AdamW fused with the NVLink gradient "
+                        "reduce-scatter and parameter gather (default on GPUs); fsdp = FSDP2 over NCCL")
+    p.add_argument("--kernel-breakdown", default=None, metavar="FILE",
+                   help="write per-kernel device time of one extra untimed step (torch profiler) as JSON")
     return p.parse_args(argv)
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks/throttle reasons while the timed region runs."""
+    """Samples nvidia-smi clocks / throttle reasons while the timed region runs.
+
+    One long-lived ``nvidia-smi -lms 200`` child started on entry and stopped on exit: sampling
+    from a thread with one ``subprocess.run`` per sample would fork this (large) process every
+    200 ms and take the interpreter lock from the thread that launches the kernels."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -61,27 +69,41 @@ class ClockSampler:
     def __init__(self, index: int) -> None:
         self.index = index
         self.samples: list[list[str]] = []
-        self._stop = threading.Event()
-        self._thread = threading.Thread(target=self._run, daemon=True)
-
-    def _run(self) -> None:
-        while not self._stop.is_set():
-            try:
-                out = subprocess.run(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
-                for line in out.stdout.strip().splitlines():
-                    self.samples.append([x.strip() for x in line.split(",")])
-            except Exception:
-                pass
-            self._stop.wait(0.2)
+        self._proc = None
 
     def __enter__(self):
-        self._thread.start()
+        import tempfile
+
+        self._log = tempfile.NamedTemporaryFile(prefix="clocks-", suffix=".csv", delete=False)
+        self._log.close()
+        try:
+            self._proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                                           "--format=csv,noheader,nounits", "-lms", "200", "-f", self._log.name],
+                                          stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL)
+        except OSError:
+            self._proc = None
         return self
 
     def __exit__(self, *exc):
-        self._stop.set()
-        self._thread.join(timeout=10)
+        import signal
+
+        if self._proc is None:
+            return
+        self._proc.send_signal(signal.SIGINT)  # the loop mode's own stop request: flushes the log
+        try:
+            self._proc.wait(timeout=10)
+        except subprocess.TimeoutExpired:
+            self._proc.kill()
+            self._proc.wait()
+        try:
+            with open(self._log.name) as f:
+                out = f.read()
+        finally:
+            os.unlink(self._log.name)
+        for line in out.strip().splitlines():
+            fields = [x.strip() for x in line.split(",")]
+            if len(fields) >= 9:
+                self.samples.append(fields)
 
     def summary(self) -> dict:
         if not self.samples:
@@ -116,8 +138,10 @@ def memory_plan(args, world: int) -> tuple[bool, str]:
     per_rank = experts / world + dense / world
     budget = HBM_BYTES - ACTIVATION_RESERVE
     choices = ("fp32", "bf16") if args.moment_dtype == "auto" else (args.moment_dtype,)
+    # dense weights kept as bf16 replicas with a staged gradient copy (peer-memory sync) instead of shards
+    replicas = dense * 4 - dense / world * 2 if getattr(args, "dense_sync", "auto") != "fsdp" else 0.0
     for moments in choices:
-        need = per_rank * (2 + 4 + (8 if moments == "fp32" else 4))
+        need = per_rank * (2 + 4 + (8 if moments == "fp32" else 4)) + replicas
         if need <= budget:
             args.moment_dtype = moments
             return True, f"{need / 2 ** 30:.0f} GiB of persistent state per rank ({moments} moments)"

@@ -45,6 +45,9 @@ def parse_args(argv=None):
     p.add_argument("--intermediate", type=int, default=768)
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--kernel-breakdown", default=None, metavar="PREFIX",
+                   help="write per-kernel device time of one extra untimed iteration of each arm to "
+                        "PREFIX.{exchange,layer}.rankR.json (torch profiler)")
     return p.parse_args(argv)
 
 
@@ -134,10 +137,15 @@ def _reference_step(args, mesh, tensors, experts):
     return step
 
 
-def _time(step, args, dev):
+def _time(step, args, dev, census_path=None):
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=dev)
     for _ in range(args.warmup):
         step()
+    if census_path:  # one extra untimed iteration under the profiler, before the timed loop
+        from tiny_dsv41_b200.utils.kernel_census import kernel_census, write_census
+
+        dist.barrier()
+        write_census(kernel_census(step), census_path, rank=dist.get_rank(), world=dist.get_world_size())
     events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.iters)]
     dist.barrier()
     torch.cuda.synchronize()
@@ -167,8 +175,9 @@ def main(argv=None) -> None:
     tensors = _inputs(args, rank, world, dev)
     make = _reference_step if args.impl == "reference" else _native_step
     try:
-        comm_us = _time(make(args, mesh, tensors, False), args, dev)
-        layer_us = _time(make(args, mesh, tensors, True), args, dev)
+        kb = args.kernel_breakdown
+        comm_us = _time(make(args, mesh, tensors, False), args, dev, kb and f"{kb}.exchange.rank{rank}.json")
+        layer_us = _time(make(args, mesh, tensors, True), args, dev, kb and f"{kb}.layer.rank{rank}.json")
         sent = _sent_bytes(tensors[2], args.experts // world, rank, world, args.hidden, args.impl == "native")
         b = torch.tensor([float(sent)], device=dev)
         dist.all_reduce(b, op=dist.ReduceOp.MAX)

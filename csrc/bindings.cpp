@@ -116,6 +116,17 @@ void ep_combine_push(const at::Tensor& y, const at::Tensor& route, const c10::op
                      const at::Tensor& peer_flags, int64_t my_rank, int64_t epoch);
 at::Tensor ep_reduce_returned(const at::Tensor& ret, const at::Tensor& dest_mask, const at::Tensor& slot,
                               int64_t tokens);
+// peer_optim.cu
+void peer_update(const at::Tensor& peer_grad, const at::Tensor& peer_param, const at::Tensor& peer_flags,
+                 const at::Tensor& my_flags, int64_t flag_row, int64_t my_rank, int64_t epoch, int64_t offset,
+                 at::Tensor& master, const c10::optional<at::Tensor>& m, const c10::optional<at::Tensor>& v,
+                 int64_t algo, double lr, double beta1, double beta2, double eps, double weight_decay, int64_t step,
+                 double grad_scale, const c10::optional<at::Tensor>& grad_scale_t,
+                 const c10::optional<at::Tensor>& nonfinite, int64_t max_blocks);
+// sparse_attention.cu
+std::vector<at::Tensor> sparse_attention_fwd(const at::Tensor& q, const at::Tensor& kv, const at::Tensor& win_idx,
+                                             const at::Tensor& win_mask, const c10::optional<at::Tensor>& comp,
+                                             const c10::optional<at::Tensor>& comp_idx, const at::Tensor& sinks);
 // fake_quant.cu
 at::Tensor cache_fake_quant(const at::Tensor& x, int64_t kind);
 // index_scores.cu
@@ -198,4 +209,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_push_rows", &tdsv::ep_push_rows);
   m.def("ep_combine_push", &tdsv::ep_combine_push);
   m.def("ep_reduce_returned", &tdsv::ep_reduce_returned);
+  m.def("peer_update", &tdsv::peer_update);
+  m.def("sparse_attention_fwd", &tdsv::sparse_attention_fwd);
 }

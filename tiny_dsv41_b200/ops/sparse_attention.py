@@ -12,9 +12,11 @@ keys (``sparse_indexer.py:156-172``), -inf outside [start, end) or outside the c
 
 On CUDA, ``index_scores`` runs the tcgen05 kernel of ``csrc/index_scores.cu`` (keys as the M
 operand, the block's (query, head) rows as N, relu / head weights / head reduction in the TMEM
-epilogue; head dim 64 or 128, heads a power of two from 4 to 64). ``sparse_attention`` is a gathered batched
-matmul (cuBLAS through PyTorch); its own kernel is not built yet. The PyTorch restatements below
-are the oracle on CPU.
+epilogue; head dim 64 or 128, heads a power of two from 4 to 64). ``sparse_attention`` runs the
+tcgen05 forward of ``csrc/sparse_attention.cu`` (gathered keys as the M operand, 64 heads as N,
+online softmax seeded with the sink; bf16, head dim 128 / 256 / 512, no dropout); its backward
+recomputes the gathered restatement below in fp32 under autograd. Other shapes run the
+restatement itself, which is also the oracle on CPU.
 """
 
 from __future__ import annotations
@@ -25,8 +27,54 @@ import torch.nn.functional as F
 from ._ext import ext, on_gpu
 
 
+def _sparse_kernel_ok(query, kv, window_indices, compressed_kv, compressed_indices, dropout) -> bool:
+    dim = query.shape[-1]
+    return (dropout == 0.0 and query.dtype == torch.bfloat16 and kv.dtype == torch.bfloat16
+            and dim in (128, 256, 512) and window_indices.shape[-1] + (
+                0 if compressed_indices is None else compressed_indices.shape[-1]) > 0
+            and (compressed_kv is None or compressed_kv.dtype == torch.bfloat16))
+
+
+class _SparseAttention(torch.autograd.Function):
+    """Kernel forward; backward by recomputing the gathered restatement under autograd."""
+
+    @staticmethod
+    def forward(ctx, query, kv, window_indices, window_mask, compressed_kv, compressed_indices, sinks):
+        q = query.transpose(1, 2).contiguous()  # [B, L, H, D]: free when the projection wrote it that way
+        comp = None if compressed_kv is None else compressed_kv.contiguous()
+        cidx = None if compressed_indices is None else compressed_indices.long().contiguous()
+        out, lse = ext().sparse_attention_fwd(q, kv.contiguous(), window_indices.long().contiguous(),
+                                              window_mask.bool().contiguous(), comp, cidx,
+                                              sinks.float().contiguous())
+        ctx.save_for_backward(query, kv, window_indices, window_mask, compressed_kv, compressed_indices, sinks)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        query, kv, window_indices, window_mask, compressed_kv, compressed_indices, sinks = ctx.saved_tensors
+        inputs = [t.detach().requires_grad_(t.requires_grad) if t is not None and t.is_floating_point() else t
+                  for t in (query, kv, compressed_kv, sinks)]
+        with torch.enable_grad():
+            out = sparse_attention_reference(inputs[0], inputs[1], window_indices, window_mask, inputs[2],
+                                             compressed_indices, inputs[3])
+            wrt = [t for t in inputs if t is not None and t.requires_grad]
+            grads = torch.autograd.grad(out, wrt, grad_out, allow_unused=True) if wrt else []
+        it = iter(grads)
+        result = [next(it) if t is not None and t.requires_grad else None for t in inputs]
+        return result[0], result[1], None, None, result[2], None, result[3]
+
+
 def sparse_attention(query, kv, window_indices, window_mask, compressed_kv, compressed_indices, sinks, *,
                      dropout: float = 0.0, deterministic: bool = False):
+    if on_gpu(query) and _sparse_kernel_ok(query, kv, window_indices, compressed_kv, compressed_indices, dropout):
+        return _SparseAttention.apply(query, kv, window_indices, window_mask, compressed_kv, compressed_indices,
+                                      sinks)
+    return sparse_attention_reference(query, kv, window_indices, window_mask, compressed_kv, compressed_indices,
+                                      sinks, dropout=dropout)
+
+
+def sparse_attention_reference(query, kv, window_indices, window_mask, compressed_kv, compressed_indices, sinks, *,
+                               dropout: float = 0.0):
     batch, heads, length, dim = query.shape
     rows = torch.arange(batch, device=query.device).view(-1, 1, 1)
     window_kv = kv[rows, window_indices.long()]  # [B, L, W, D]
@@ -82,4 +130,4 @@ def index_scores_reference(query, keys, weights, starts, ends, width, candidates
     return scores.masked_fill(~valid, float("-inf"))
 
 
-__all__ = ["index_scores", "index_scores_reference", "sparse_attention"]
+__all__ = ["index_scores", "index_scores_reference", "sparse_attention", "sparse_attention_reference"]

@@ -5,7 +5,9 @@ Each parameter (or its local FSDP/DTensor shard) gets an fp32 master copy and tw
 decoupled weight decay, updates the moments with bias correction (``torch.optim.AdamW``
 semantics), writes the new master and the rounded bf16 parameter. With ``in_backward=True`` the
 update of a parameter runs from its post-accumulate-grad hook, so gradients never accumulate for
-the whole model (no global-norm clipping in that mode).
+the whole model (no global-norm clipping in that mode). ``side_stream=True`` runs those updates on
+a stream of their own, so the memory-bound update of one parameter overlaps the backward GEMMs of
+the next; ``finish_step()`` then orders the caller's stream after them.
 
 On CPU the same math runs in plain PyTorch.
 """
@@ -23,7 +25,7 @@ from ..runtime import local_tensor
 class FusedAdamW:
     def __init__(self, params, lr: float = 1e-4, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.01, *, moment_dtype: torch.dtype = torch.float32,
-                 in_backward: bool = False, grad_scale: float = 1.0) -> None:
+                 in_backward: bool = False, grad_scale: float = 1.0, side_stream: bool = False) -> None:
         self.params = [p for p in params if p.requires_grad]
         self.lr, self.betas, self.eps, self.weight_decay = lr, betas, eps, weight_decay
         self.moment_dtype = moment_dtype
@@ -38,6 +40,8 @@ class FusedAdamW:
                 "v": torch.zeros(local.shape, dtype=moment_dtype, device=local.device),
             }
         self.in_backward = in_backward
+        device = self.params[0].device if self.params else torch.device("cpu")
+        self.stream = torch.cuda.Stream(device=device) if side_stream and device.type == "cuda" else None
         self._hooks = []
         self._pending_step = False
         if in_backward:
@@ -52,6 +56,11 @@ class FusedAdamW:
     def begin_step(self) -> None:
         """In-backward mode: advance the step counter before the backward that applies it."""
         self.step_count += 1
+
+    def finish_step(self) -> None:
+        """Order the current stream after the updates queued on the side stream (no-op without one)."""
+        if self.stream is not None:
+            torch.cuda.current_stream(self.stream.device).wait_stream(self.stream)
 
     def step(self, clip_coefficient: torch.Tensor | None = None) -> None:
         if self.in_backward:
@@ -81,7 +90,14 @@ class FusedAdamW:
     def _hook(self, p: torch.Tensor) -> None:
         if self.step_count == 0:
             self.step_count = 1
-        self._update(p, None)
+        if self.stream is not None:
+            self.stream.wait_stream(torch.cuda.current_stream(self.stream.device))
+            grad = local_tensor(p.grad)
+            with torch.cuda.stream(self.stream):
+                self._update(p, None)
+            grad.record_stream(self.stream)  # the gradient's memory outlives its use on the side stream
+        else:
+            self._update(p, None)
         p.grad = None
 
     @torch.no_grad()

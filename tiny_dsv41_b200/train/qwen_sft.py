@@ -1,8 +1,11 @@
 """Qwen3-MoE full-parameter trainer (the public training API) and its benchmark harness.
 
 :class:`QwenTrainer` builds the model directly on the GPU (meta-device construction, then
-random init on the device), shards dense weights with FSDP2 over the world and places experts
-with EP, and runs AdamW with fp32 master weights applied inside the backward pass.
+random init on the device), places experts with EP, keeps dense weights as bf16 replicas whose
+fp32 master and AdamW moments are sharded over the world (``parallel/peer_fsdp.py``: one NVLink
+kernel per layer reduces the gradient, updates the shard and writes the new weights to every
+rank; ``dense_sync="fsdp"`` selects FSDP2 over NCCL instead), and applies AdamW with fp32 master
+weights inside the backward pass.
 ``train_step(input_ids, labels)`` is one optimizer step; inputs may live on the host (pinned) or
 the device.
 
@@ -15,6 +18,7 @@ from __future__ import annotations
 
 import os
 import time
+import zlib
 
 import torch
 import torch.distributed as dist
@@ -40,14 +44,14 @@ def _init_on_device(model: Qwen3MoeForCausalLM, seed: int, rank: int) -> None:
                 p.zero_()
             else:
                 is_expert = ".experts." in name
-                gen.manual_seed(seed + (1000003 * (rank + 1) if is_expert else 0) + hash(name) % 100003)
+                gen.manual_seed(seed + (1000003 * (rank + 1) if is_expert else 0) + zlib.crc32(name.encode()) % 100003)
                 p.normal_(0.0, std, generator=gen)
 
 
 class QwenTrainer:
     def __init__(self, config: Qwen3MoeConfig, *, lr: float = 1e-5, moment_dtype=torch.float32,
                  dispatcher: str = "auto", gradient_checkpointing: bool = True, seed: int = 0,
-                 tokens_per_rank: int = 4096, cp_size: int = 1) -> None:
+                 tokens_per_rank: int = 4096, cp_size: int = 1, dense_sync: str = "auto") -> None:
         self.runtime = initialize_runtime(require_distributed=int(os.environ.get("WORLD_SIZE", "1")) > 1,
                                           timeout_seconds=900)
         rt = self.runtime
@@ -75,16 +79,30 @@ class QwenTrainer:
         model.train()
         self.expert_params = [p for m in model.modules() if isinstance(m, Qwen3MoeExperts) for p in m.parameters()]
         expert_ids = {id(p) for p in self.expert_params}
-        if self.world > 1:
+        # dense weights: "peer" = bf16 replicas with a sharded optimizer fused with the gradient
+        # reduce-scatter and the parameter all-gather over NVLink (parallel/peer_fsdp.py);
+        # "fsdp" = FSDP2 over NCCL (the reference's scheme)
+        if dense_sync == "auto":
+            dense_sync = "peer" if rt.device.type == "cuda" else ("fsdp" if self.world > 1 else "local")
+        self.dense_sync = dense_sync if self.world > 1 or dense_sync == "peer" else "local"
+        if self.world > 1 and self.dense_sync == "fsdp":
             self._apply_fsdp(model)
         self.model = model
-        dense = [p for p in model.parameters() if id(p) not in expert_ids]
         # device status word (bounded peer waits, bounds checks) read once per step by the loops
         self.monitor = StatusMonitor(rt.device)
+        hyper = dict(lr=lr, betas=(0.9, 0.95), weight_decay=0.1, moment_dtype=moment_dtype)
+        side = rt.device.type == "cuda"
+        if self.dense_sync == "peer":
+            from ..parallel.peer_fsdp import PeerShardedOptimizer, decoder_units
+
+            dense_opt = PeerShardedOptimizer(decoder_units(model, expert_ids), algo="adamw", **hyper)
+        else:
+            dense = [p for p in model.parameters() if id(p) not in expert_ids]
+            # under FSDP the update follows FSDP's own reduce-scatter stream; it stays on the default stream
+            dense_opt = FusedAdamW(dense, in_backward=True, side_stream=side and self.dense_sync != "fsdp", **hyper)
         self.optimizers = [
-            FusedAdamW(dense, lr=lr, betas=(0.9, 0.95), weight_decay=0.1, moment_dtype=moment_dtype, in_backward=True),
-            FusedAdamW(self.expert_params, lr=lr, betas=(0.9, 0.95), weight_decay=0.1, moment_dtype=moment_dtype,
-                       in_backward=True, grad_scale=1.0 / self.world),
+            dense_opt,
+            FusedAdamW(self.expert_params, in_backward=True, grad_scale=1.0 / self.world, side_stream=side, **hyper),
         ]
 
     def _make_dispatcher(self, kind: str):
@@ -135,6 +153,8 @@ class QwenTrainer:
             opt.begin_step()
         out = self.model(input_ids, labels=labels, output_router_logits=True)
         out.loss.backward()
+        for opt in self.optimizers:
+            opt.finish_step()
         return out.loss.detach()
 
     def close(self) -> None:
@@ -152,7 +172,8 @@ class QwenSFTBench:
         moment = torch.float32 if args.moment_dtype == "fp32" else torch.bfloat16
         self.cp = getattr(args, "cp", 1)
         self.trainer = QwenTrainer(config, lr=args.lr, moment_dtype=moment, dispatcher=args.dispatcher,
-                                   tokens_per_rank=args.batch_size * args.seq_len // self.cp, cp_size=self.cp)
+                                   tokens_per_rank=args.batch_size * args.seq_len // self.cp, cp_size=self.cp,
+                                   dense_sync=getattr(args, "dense_sync", "auto"))
         self.config = config
 
     def _batch(self, gen: torch.Generator):
@@ -165,20 +186,14 @@ class QwenSFTBench:
 
     def _count_launches(self, batches) -> dict:
         """Kernels launched in one (extra, untimed) step, split into this repo's and others."""
-        from torch.profiler import ProfilerActivity, profile
+        from ..utils.kernel_census import kernel_census, write_census
 
         ids, labels = batches[0]
-        with profile(activities=[ProfilerActivity.CUDA]) as prof:
-            self.trainer.train_step(ids, labels)
-            torch.cuda.synchronize()
-        own = other = 0
-        for evt in prof.events():
-            if evt.device_type == torch.autograd.DeviceType.CUDA:
-                if "tdsv" in evt.name:
-                    own += 1
-                else:
-                    other += 1
-        return {"own": own, "other": other}
+        census = kernel_census(lambda: self.trainer.train_step(ids, labels))
+        path = getattr(self.args, "kernel_breakdown", None)
+        if path and self.trainer.runtime.rank == 0:
+            write_census(census, path, rank=0, world=self.trainer.world)
+        return {"own": census["own"], "other": census["other"]}
 
     def run(self) -> dict:
         import sys
@@ -209,10 +224,12 @@ class QwenSFTBench:
         with ClockSampler(rt.local_rank) as clocks:
             barrier()
             start.record()
+            host0 = time.perf_counter()
             for i in range(a.steps):
                 flush.zero_()
                 losses.append(t.train_step(*batches[i % len(batches)]))
             end.record()
+            host_ms = (time.perf_counter() - host0) * 1000.0  # time to enqueue the K steps (no sync inside)
             barrier()
         device_ms = start.elapsed_time(end)
         t.monitor.step_end("timed steps")
@@ -230,10 +247,10 @@ class QwenSFTBench:
         # kernel census of one more (untimed) step of the same shape; after the timed loops, so the
         # profiler's instrumentation cannot touch them
         launches = self._count_launches(batches)
-        times = torch.tensor([device_ms, wall_s * 1000.0, peak_gib], device=rt.device)
+        times = torch.tensor([device_ms, wall_s * 1000.0, peak_gib, host_ms], device=rt.device)
         if dist.is_initialized():
             dist.all_reduce(times, op=dist.ReduceOp.MAX)
-        device_ms, wall_ms, peak_gib = times.tolist()
+        device_ms, wall_ms, peak_gib, host_ms = times.tolist()
         tokens = a.batch_size * a.seq_len * (rt.world_size // self.cp) * a.steps
         value = tokens / (device_ms / 1000.0)
         e2e = tokens / (wall_ms / 1000.0)
@@ -248,13 +265,16 @@ class QwenSFTBench:
             "loss": final_loss,
             "e2e_last_loss": e2e_losses[-1],
             "peak_memory_gib": round(peak_gib, 2),
+            "host_enqueue_ms_per_step": round(host_ms / a.steps, 1),
             "clocks": clocks.summary(),
             "config": {
                 "model": MODEL_NAME if self.config.num_hidden_layers == 48 else f"REDUCED {self.config.num_hidden_layers}L (not the benchmark)",
                 "global_batch": a.batch_size * rt.world_size // self.cp, "seq_len": a.seq_len,
-                "parallelism": ((f"cp{self.cp}+" if self.cp > 1 else "") + f"ep{rt.world_size}+fsdp{rt.world_size}"
+                "parallelism": ((f"cp{self.cp}+" if self.cp > 1 else "") + f"ep{rt.world_size}+"
+                                + ("dp" if t.dense_sync == "peer" else "fsdp") + f"{rt.world_size}"
                                 if rt.world_size > 1 else "single-gpu"),
                 "optimizer": f"AdamW in-backward, fp32 master, {a.moment_dtype} moments",
+                "dense_sync": t.dense_sync,
                 "grad_ckpt": True, "l2": "256 MB buffer written between timed steps",
                 "loss_tokens": "last 50%",
             },
