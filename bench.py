@@ -50,9 +50,15 @@ def parse_args(argv=None):
     p.add_argument("--dense-sync", choices=("auto", "peer", "fsdp"), default="auto",
                    help="dense weights: peer = bf16 replicas + sharded AdamW fused with the NVLink gradient "
                         "reduce-scatter and parameter gather (default on GPUs); fsdp = FSDP2 over NCCL")
+    p.add_argument("--cuda-graph", action=argparse.BooleanOptionalAction, default=None,
+                   help="replay each training step as one captured CUDA graph (default: on when the step "
+                        "has no NCCL call, i.e. --cp 1 and peer dense sync)")
     p.add_argument("--kernel-breakdown", default=None, metavar="FILE",
                    help="write per-kernel device time of one extra untimed step (torch profiler) as JSON")
-    return p.parse_args(argv)
+    args = p.parse_args(argv)
+    if args.cuda_graph is None:
+        args.cuda_graph = args.cp == 1 and args.dense_sync != "fsdp"
+    return args
 
 
 class ClockSampler:

@@ -82,7 +82,8 @@ at::Tensor token_logprob_bwd(const at::Tensor& logits, const at::Tensor& targets
 // optim.cu
 void adamw_step(at::Tensor& master, const at::Tensor& grad, at::Tensor& m, at::Tensor& v,
                 const c10::optional<at::Tensor>& out, double lr, double beta1, double beta2, double eps,
-                double weight_decay, int64_t step, double grad_scale, const c10::optional<at::Tensor>& grad_scale_t);
+                double weight_decay, int64_t step, double grad_scale, const c10::optional<at::Tensor>& grad_scale_t,
+                const c10::optional<at::Tensor>& step_t);
 void sgd_step(at::Tensor& param, const at::Tensor& grad, const c10::optional<at::Tensor>& out, double lr,
               double grad_scale, const c10::optional<at::Tensor>& nonfinite);
 at::Tensor grad_sq_norm(const at::Tensor& g);
@@ -101,19 +102,21 @@ at::Tensor mhc_expand_fwd(const at::Tensor& v, const at::Tensor& r, const at::Te
 std::vector<at::Tensor> mhc_expand_bwd(const at::Tensor& g, const at::Tensor& v, const at::Tensor& r,
                                        const at::Tensor& post, const at::Tensor& comb);
 // ep_nvlink.cu
-void ep_wait(const at::Tensor& flags, int64_t epoch);
+void ep_wait(const at::Tensor& flags, int64_t epoch, const c10::optional<at::Tensor>& epoch_base);
 void ep_signal(const at::Tensor& peer_flags, const c10::optional<at::Tensor>& peer_counts,
-               const c10::optional<at::Tensor>& counts, int64_t my_rank, int64_t epoch);
+               const c10::optional<at::Tensor>& counts, int64_t my_rank, int64_t epoch,
+               const c10::optional<at::Tensor>& epoch_base);
 void ep_push_rows(const at::Tensor& x, const at::Tensor& dest_mask, const at::Tensor& slot,
                   const at::Tensor& peer_recv, const c10::optional<at::Tensor>& peer_meta,
                   const c10::optional<at::Tensor>& ids, const c10::optional<at::Tensor>& weights, int64_t t_cap,
                   int64_t e_local, at::Tensor& done_counter, const at::Tensor& peer_flags,
                   const c10::optional<at::Tensor>& peer_counts, const c10::optional<at::Tensor>& counts,
-                  int64_t my_rank, int64_t epoch);
+                  int64_t my_rank, int64_t epoch, const c10::optional<at::Tensor>& epoch_base);
 void ep_combine_push(const at::Tensor& y, const at::Tensor& route, const c10::optional<at::Tensor>& weights,
                      const at::Tensor& counts, const at::Tensor& peer_ret, const c10::optional<at::Tensor>& row_extra,
                      const c10::optional<at::Tensor>& peer_retw, int64_t t_cap, at::Tensor& done_counter,
-                     const at::Tensor& peer_flags, int64_t my_rank, int64_t epoch);
+                     const at::Tensor& peer_flags, int64_t my_rank, int64_t epoch,
+                     const c10::optional<at::Tensor>& epoch_base);
 at::Tensor ep_reduce_returned(const at::Tensor& ret, const at::Tensor& dest_mask, const at::Tensor& slot,
                               int64_t tokens);
 // peer_optim.cu
@@ -122,11 +125,17 @@ void peer_update(const at::Tensor& peer_grad, const at::Tensor& peer_param, cons
                  at::Tensor& master, const c10::optional<at::Tensor>& m, const c10::optional<at::Tensor>& v,
                  int64_t algo, double lr, double beta1, double beta2, double eps, double weight_decay, int64_t step,
                  double grad_scale, const c10::optional<at::Tensor>& grad_scale_t,
-                 const c10::optional<at::Tensor>& nonfinite, int64_t max_blocks);
+                 const c10::optional<at::Tensor>& nonfinite, int64_t max_blocks,
+                 const c10::optional<at::Tensor>& step_t, const c10::optional<at::Tensor>& epoch_base);
 // sparse_attention.cu
 std::vector<at::Tensor> sparse_attention_fwd(const at::Tensor& q, const at::Tensor& kv, const at::Tensor& win_idx,
                                              const at::Tensor& win_mask, const c10::optional<at::Tensor>& comp,
                                              const c10::optional<at::Tensor>& comp_idx, const at::Tensor& sinks);
+std::vector<at::Tensor> sparse_attention_bwd(const at::Tensor& q, const at::Tensor& kv, const at::Tensor& win_idx,
+                                             const at::Tensor& win_mask, const c10::optional<at::Tensor>& comp,
+                                             const c10::optional<at::Tensor>& comp_idx, const at::Tensor& sinks,
+                                             const at::Tensor& out, const at::Tensor& lse, const at::Tensor& dout,
+                                             c10::optional<int64_t> ordered_chunk);
 // fake_quant.cu
 at::Tensor cache_fake_quant(const at::Tensor& x, int64_t kind);
 // index_scores.cu
@@ -192,7 +201,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cross_entropy_fused", &tdsv::cross_entropy_fused);
   m.def("token_logprob_fwd", &tdsv::token_logprob_fwd);
   m.def("token_logprob_bwd", &tdsv::token_logprob_bwd);
-  m.def("adamw_step", &tdsv::adamw_step);
+  m.def("adamw_step", &tdsv::adamw_step, py::arg("master"), py::arg("grad"), py::arg("m"), py::arg("v"),
+        py::arg("out"), py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("weight_decay"),
+        py::arg("step"), py::arg("grad_scale"), py::arg("grad_scale_t"), py::arg("step_t") = py::none());
   m.def("sgd_step", &tdsv::sgd_step);
   m.def("grad_sq_norm", &tdsv::grad_sq_norm);
   m.def("gemm", &tdsv::gemm);
@@ -204,11 +215,27 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mhc_collapse_bwd", &tdsv::mhc_collapse_bwd);
   m.def("mhc_expand_fwd", &tdsv::mhc_expand_fwd);
   m.def("mhc_expand_bwd", &tdsv::mhc_expand_bwd);
-  m.def("ep_wait", &tdsv::ep_wait);
-  m.def("ep_signal", &tdsv::ep_signal);
-  m.def("ep_push_rows", &tdsv::ep_push_rows);
-  m.def("ep_combine_push", &tdsv::ep_combine_push);
+  // the trailing epoch_base (device int32 scalar added to the epoch) is optional
+  m.def("ep_wait", &tdsv::ep_wait, py::arg("flags"), py::arg("epoch"), py::arg("epoch_base") = py::none());
+  m.def("ep_signal", &tdsv::ep_signal, py::arg("peer_flags"), py::arg("peer_counts"), py::arg("counts"),
+        py::arg("my_rank"), py::arg("epoch"), py::arg("epoch_base") = py::none());
+  m.def("ep_push_rows", &tdsv::ep_push_rows, py::arg("x"), py::arg("dest_mask"), py::arg("slot"), py::arg("peer_recv"),
+        py::arg("peer_meta"), py::arg("ids"), py::arg("weights"), py::arg("t_cap"), py::arg("e_local"),
+        py::arg("done_counter"), py::arg("peer_flags"), py::arg("peer_counts"), py::arg("counts"), py::arg("my_rank"),
+        py::arg("epoch"), py::arg("epoch_base") = py::none());
+  m.def("ep_combine_push", &tdsv::ep_combine_push, py::arg("y"), py::arg("route"), py::arg("weights"),
+        py::arg("counts"), py::arg("peer_ret"), py::arg("row_extra"), py::arg("peer_retw"), py::arg("t_cap"),
+        py::arg("done_counter"), py::arg("peer_flags"), py::arg("my_rank"), py::arg("epoch"),
+        py::arg("epoch_base") = py::none());
   m.def("ep_reduce_returned", &tdsv::ep_reduce_returned);
-  m.def("peer_update", &tdsv::peer_update);
+  m.def("peer_update", &tdsv::peer_update, py::arg("peer_grad"), py::arg("peer_param"), py::arg("peer_flags"),
+        py::arg("my_flags"), py::arg("flag_row"), py::arg("my_rank"), py::arg("epoch"), py::arg("offset"),
+        py::arg("master"), py::arg("m"), py::arg("v"), py::arg("algo"), py::arg("lr"), py::arg("beta1"),
+        py::arg("beta2"), py::arg("eps"), py::arg("weight_decay"), py::arg("step"), py::arg("grad_scale"),
+        py::arg("grad_scale_t"), py::arg("nonfinite"), py::arg("max_blocks"), py::arg("step_t") = py::none(),
+        py::arg("epoch_base") = py::none());
   m.def("sparse_attention_fwd", &tdsv::sparse_attention_fwd);
+  m.def("sparse_attention_bwd", &tdsv::sparse_attention_bwd, py::arg("q"), py::arg("kv"), py::arg("win_idx"),
+        py::arg("win_mask"), py::arg("comp"), py::arg("comp_idx"), py::arg("sinks"), py::arg("out"), py::arg("lse"),
+        py::arg("dout"), py::arg("ordered_chunk") = py::none());
 }

@@ -31,11 +31,19 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
   return v;
 }
 
+// Epoch of an exchange: `offset` alone, or added to a device-resident base. With a base the host
+// passes per-step offsets and advances the base once per step on the stream, so a captured CUDA
+// graph replays with fresh epochs instead of the ones baked in at capture.
+__device__ __forceinline__ uint32_t epoch_at(const uint32_t* base, uint32_t offset) {
+  return base == nullptr ? offset : *reinterpret_cast<const volatile uint32_t*>(base) + offset;
+}
+
 // Wait until flags[s] >= epoch for every s != skip (or all s). One thread per source.
-__global__ void wait_flags_kernel(const uint32_t* __restrict__ flags, int ep, uint32_t epoch, int* status,
-                                  uint64_t limit_ns) {
+__global__ void wait_flags_kernel(const uint32_t* __restrict__ flags, int ep, const uint32_t* base, uint32_t offset,
+                                  int* status, uint64_t limit_ns) {
   const int s = threadIdx.x;
   if (s >= ep) return;
+  const uint32_t epoch = epoch_at(base, offset);
   const uint64_t start = global_timer_ns();
   for (uint32_t i = 0;; ++i) {
     if (static_cast<int32_t>(ld_acquire_sys(flags + s) - epoch) >= 0) return;
@@ -48,9 +56,11 @@ __global__ void wait_flags_kernel(const uint32_t* __restrict__ flags, int ep, ui
 
 // Raise flag slot `my_rank` of every peer's flag array to `epoch` (optionally writing counts first).
 __global__ void signal_peers_kernel(const int64_t* __restrict__ peer_flags, const int64_t* __restrict__ peer_counts,
-                                    const int32_t* __restrict__ counts, int ep, int my_rank, uint32_t epoch) {
+                                    const int32_t* __restrict__ counts, int ep, int my_rank, const uint32_t* base,
+                                    uint32_t offset) {
   const int d = threadIdx.x;
   if (d >= ep) return;
+  const uint32_t epoch = epoch_at(base, offset);
   __threadfence_system();
   if (peer_counts != nullptr) {
     reinterpret_cast<int32_t*>(peer_counts[d])[my_rank] = counts[d];
@@ -67,7 +77,8 @@ __global__ void push_rows_kernel(const __nv_bfloat16* __restrict__ x, const uint
                                  const float* __restrict__ weights, int64_t tokens, int h, int ep, int my_rank,
                                  int64_t t_cap, int k, int e_local, unsigned int* __restrict__ done_counter,
                                  const int64_t* __restrict__ peer_flags, const int64_t* __restrict__ peer_counts,
-                                 const int32_t* __restrict__ counts, uint32_t epoch, int* status) {
+                                 const int32_t* __restrict__ counts, const uint32_t* base, uint32_t offset,
+                                 int* status) {
   const int lane = threadIdx.x & 31;
   const int64_t t = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (t < tokens) {
@@ -97,6 +108,7 @@ __global__ void push_rows_kernel(const __nv_bfloat16* __restrict__ x, const uint
     const unsigned int prev = atomicAdd(done_counter, 1u);
     if (prev == gridDim.x - 1) {
       *done_counter = 0;  // reset for the next launch (stream order protects reuse)
+      const uint32_t epoch = epoch_at(base, offset);
       __threadfence_system();
       for (int d = 0; d < ep; ++d) {
         if (peer_counts != nullptr) reinterpret_cast<int32_t*>(peer_counts[d])[my_rank] = counts[d];
@@ -107,6 +119,8 @@ __global__ void push_rows_kernel(const __nv_bfloat16* __restrict__ x, const uint
   }
 }
 
+constexpr int kCombineWarps = 8;  // warps per block of combine_push_kernel (one received row each)
+
 // For every received row (source s, index i < counts[s]) compute sum_j w_j * y[route[s,i,j]]
 // (fp32; w = 1 when weights is null) and store it into source s's ret slab `my_rank`, row i.
 __global__ void combine_push_kernel(const __nv_bfloat16* __restrict__ y, const int32_t* __restrict__ route,
@@ -114,22 +128,50 @@ __global__ void combine_push_kernel(const __nv_bfloat16* __restrict__ y, const i
                                     const int64_t* __restrict__ peer_ret, const float* __restrict__ row_extra,
                                     const int64_t* __restrict__ peer_retw, int64_t t_cap, int h, int ep, int my_rank,
                                     int k, unsigned int* __restrict__ done_counter,
-                                    const int64_t* __restrict__ peer_flags, uint32_t epoch, int64_t y_rows,
-                                    int* status) {
-  const int lane = threadIdx.x & 31;
-  const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+                                    const int64_t* __restrict__ peer_flags, const uint32_t* base, uint32_t offset,
+                                    int64_t y_rows, int* status) {
+  __shared__ int s_rows[kCombineWarps][32];
+  __shared__ float s_w[kCombineWarps][32];
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + wib;
   const int s = static_cast<int>(r / t_cap);
   const int64_t i = r % t_cap;
   if (s < ep && i < counts[s]) {
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(peer_ret[s]) + (static_cast<int64_t>(my_rank) * t_cap + i) * h;
+    // the row's routes, compacted once (in route order) into a per-warp table
+    int my_row = -1;
+    float my_w = 0.f;
+    if (lane < k) {
+      my_row = route[r * k + lane];
+      my_w = weights != nullptr ? weights[r * k + lane] : 1.f;
+      if (my_row >= 0 && !TDSV_IN_BOUNDS(my_row < y_rows, status)) my_row = -1;
+    }
+    const unsigned valid = __ballot_sync(0xffffffffu, my_row >= 0);
+    if (my_row >= 0) {
+      const int slot = __popc(valid & ((1u << lane) - 1u));
+      s_rows[wib][slot] = my_row;
+      s_w[wib][slot] = my_w;
+    }
+    __syncwarp();
+    const int n = __popc(valid);
     for (int c = lane * 8; c < h; c += 256) {
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      for (int j = 0; j < k; ++j) {
-        const int row = route[r * k + j];
-        if (row < 0 || !TDSV_IN_BOUNDS(row < y_rows, status)) continue;
-        const float w = weights != nullptr ? weights[r * k + j] : 1.f;
+      int j = 0;
+      for (; j + 4 <= n; j += 4) {  // four independent 16-byte loads in flight per lane
+        float v[4][8];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) load_bf16x8(y + static_cast<int64_t>(s_rows[wib][j + u]) * h + c, v[u]);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float w = s_w[wib][j + u];
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[q] += w * v[u][q];
+        }
+      }
+      for (; j < n; ++j) {
         float v[8];
-        load_bf16x8(y + static_cast<int64_t>(row) * h + c, v);
+        load_bf16x8(y + static_cast<int64_t>(s_rows[wib][j]) * h + c, v);
+        const float w = s_w[wib][j];
 #pragma unroll
         for (int q = 0; q < 8; ++q) acc[q] += w * v[q];
       }
@@ -147,6 +189,7 @@ __global__ void combine_push_kernel(const __nv_bfloat16* __restrict__ y, const i
     const unsigned int prev = atomicAdd(done_counter, 1u);
     if (prev == gridDim.x - 1) {
       *done_counter = 0;
+      const uint32_t epoch = epoch_at(base, offset);
       __threadfence_system();
       for (int d = 0; d < ep; ++d) st_release_sys(reinterpret_cast<uint32_t*>(peer_flags[d]) + my_rank, epoch);
     }
@@ -176,22 +219,33 @@ __global__ void reduce_returned_kernel(const __nv_bfloat16* __restrict__ ret, co
 }
 
 constexpr int kWarpsPerBlock = 8;
+static_assert(kWarpsPerBlock == kCombineWarps, "combine_push_kernel's route tables are sized per warp");
 
 }  // namespace
 
-void ep_wait(const at::Tensor& flags, int64_t epoch) {
+namespace {
+const uint32_t* epoch_base_ptr(const c10::optional<at::Tensor>& base) {
+  if (!base.has_value() || !base->defined()) return nullptr;
+  check_cuda_tensor(*base, "epoch_base");
+  TDSV_CHECK(base->scalar_type() == at::kInt && base->numel() >= 1, "epoch_base: int32 device scalar");
+  return reinterpret_cast<const uint32_t*>(base->data_ptr());
+}
+}  // namespace
+
+void ep_wait(const at::Tensor& flags, int64_t epoch, const c10::optional<at::Tensor>& epoch_base) {
   check_cuda_tensor(flags, "flags");
   const int ep = static_cast<int>(flags.numel());
   TDSV_CHECK(ep <= 1024, "ep_wait: too many ranks");
   c10::cuda::CUDAGuard guard(flags.device());
   wait_flags_kernel<<<1, std::max(32, ep), 0, stream()>>>(reinterpret_cast<const uint32_t*>(flags.data_ptr()), ep,
-                                                          static_cast<uint32_t>(epoch), status_word_ptr(),
-                                                          peer_wait_limit_ns());
+                                                          epoch_base_ptr(epoch_base), static_cast<uint32_t>(epoch),
+                                                          status_word_ptr(), peer_wait_limit_ns());
   TDSV_LAUNCH_CHECK();
 }
 
 void ep_signal(const at::Tensor& peer_flags, const c10::optional<at::Tensor>& peer_counts,
-               const c10::optional<at::Tensor>& counts, int64_t my_rank, int64_t epoch) {
+               const c10::optional<at::Tensor>& counts, int64_t my_rank, int64_t epoch,
+               const c10::optional<at::Tensor>& epoch_base) {
   check_cuda_tensor(peer_flags, "peer_flags");
   const int ep = static_cast<int>(peer_flags.numel());
   const int64_t* pc = nullptr;
@@ -202,7 +256,8 @@ void ep_signal(const at::Tensor& peer_flags, const c10::optional<at::Tensor>& pe
   }
   c10::cuda::CUDAGuard guard(peer_flags.device());
   signal_peers_kernel<<<1, std::max(32, ep), 0, stream()>>>(peer_flags.data_ptr<int64_t>(), pc, cnt, ep,
-                                                            static_cast<int>(my_rank), static_cast<uint32_t>(epoch));
+                                                            static_cast<int>(my_rank), epoch_base_ptr(epoch_base),
+                                                            static_cast<uint32_t>(epoch));
   TDSV_LAUNCH_CHECK();
 }
 
@@ -211,7 +266,7 @@ void ep_push_rows(const at::Tensor& x, const at::Tensor& dest_mask, const at::Te
                   const c10::optional<at::Tensor>& ids, const c10::optional<at::Tensor>& weights, int64_t t_cap,
                   int64_t e_local, at::Tensor& done_counter, const at::Tensor& peer_flags,
                   const c10::optional<at::Tensor>& peer_counts, const c10::optional<at::Tensor>& counts,
-                  int64_t my_rank, int64_t epoch) {
+                  int64_t my_rank, int64_t epoch, const c10::optional<at::Tensor>& epoch_base) {
   check_cuda_tensor(x, "x");
   const int64_t tokens = x.size(0);
   const int h = static_cast<int>(x.size(1));
@@ -241,20 +296,23 @@ void ep_push_rows(const at::Tensor& x, const at::Tensor& dest_mask, const at::Te
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), dest_mask.data_ptr<uint8_t>(), slot.data_ptr<int32_t>(),
       peer_recv.data_ptr<int64_t>(), meta, idp, wp, tokens, h, ep, static_cast<int>(my_rank), t_cap, k,
       static_cast<int>(e_local), reinterpret_cast<unsigned int*>(done_counter.data_ptr()),
-      peer_flags.data_ptr<int64_t>(), pc, cnt, static_cast<uint32_t>(epoch), status_word_ptr());
+      peer_flags.data_ptr<int64_t>(), pc, cnt, epoch_base_ptr(epoch_base), static_cast<uint32_t>(epoch),
+      status_word_ptr());
   TDSV_LAUNCH_CHECK();
 }
 
 void ep_combine_push(const at::Tensor& y, const at::Tensor& route, const c10::optional<at::Tensor>& weights,
                      const at::Tensor& counts, const at::Tensor& peer_ret, const c10::optional<at::Tensor>& row_extra,
                      const c10::optional<at::Tensor>& peer_retw, int64_t t_cap, at::Tensor& done_counter,
-                     const at::Tensor& peer_flags, int64_t my_rank, int64_t epoch) {
+                     const at::Tensor& peer_flags, int64_t my_rank, int64_t epoch,
+                     const c10::optional<at::Tensor>& epoch_base) {
   check_cuda_tensor(y, "y");
   check_cuda_tensor(route, "route");
   const int h = static_cast<int>(y.size(1));
   const int ep = static_cast<int>(counts.numel());
   const int k = static_cast<int>(route.size(1));
   TDSV_CHECK(route.size(0) == ep * t_cap, "ep_combine_push: route must be [ep * t_cap, k]");
+  TDSV_CHECK(k >= 1 && k <= 32, "ep_combine_push: 1 <= k <= 32");
   const float* wp = nullptr;
   if (weights.has_value() && weights->defined()) wp = weights->data_ptr<float>();
   const float* extra = nullptr;
@@ -272,7 +330,7 @@ void ep_combine_push(const at::Tensor& y, const at::Tensor& route, const c10::op
       reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), route.data_ptr<int32_t>(), wp, counts.data_ptr<int32_t>(),
       peer_ret.data_ptr<int64_t>(), extra, retw, t_cap, h, ep, static_cast<int>(my_rank), k,
       reinterpret_cast<unsigned int*>(done_counter.data_ptr()), peer_flags.data_ptr<int64_t>(),
-      static_cast<uint32_t>(epoch), y.size(0), status_word_ptr());
+      epoch_base_ptr(epoch_base), static_cast<uint32_t>(epoch), y.size(0), status_word_ptr());
   TDSV_LAUNCH_CHECK();
 }
 

@@ -54,8 +54,14 @@ template <typename GT, typename MT>
 __global__ void adamw_kernel(float* __restrict__ master, const GT* __restrict__ grad, MT* __restrict__ m,
                              MT* __restrict__ v, __nv_bfloat16* __restrict__ out, int64_t n, float lr, float beta1,
                              float beta2, float eps, float weight_decay, float bc1, float bc2_sqrt,
-                             float grad_scale, const float* __restrict__ grad_scale_ptr, bool vectorized) {
+                             float grad_scale, const float* __restrict__ grad_scale_ptr, bool vectorized,
+                             const int* __restrict__ step_ptr) {
   const float gs = grad_scale * (grad_scale_ptr != nullptr ? *grad_scale_ptr : 1.f);
+  if (step_ptr != nullptr) {  // step count kept on the device (CUDA-graph replays): bias corrections here
+    const double st = static_cast<double>(*step_ptr);
+    bc1 = static_cast<float>(1.0 - pow(static_cast<double>(beta1), st));
+    bc2_sqrt = static_cast<float>(sqrt(1.0 - pow(static_cast<double>(beta2), st)));
+  }
   const float step_size = lr / bc1;
   const float decay = 1.f - lr * weight_decay;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -135,7 +141,8 @@ int grid_for(int64_t n) {
 
 void adamw_step(at::Tensor& master, const at::Tensor& grad, at::Tensor& m, at::Tensor& v,
                 const c10::optional<at::Tensor>& out, double lr, double beta1, double beta2, double eps,
-                double weight_decay, int64_t step, double grad_scale, const c10::optional<at::Tensor>& grad_scale_t) {
+                double weight_decay, int64_t step, double grad_scale, const c10::optional<at::Tensor>& grad_scale_t,
+                const c10::optional<at::Tensor>& step_t) {
   check_cuda_tensor(master, "master");
   check_cuda_tensor(grad, "grad");
   check_cuda_tensor(m, "m");
@@ -152,6 +159,12 @@ void adamw_step(at::Tensor& master, const at::Tensor& grad, at::Tensor& m, at::T
   }
   const float* gsp = nullptr;
   if (grad_scale_t.has_value() && grad_scale_t->defined()) gsp = grad_scale_t->data_ptr<float>();
+  const int* stp = nullptr;
+  if (step_t.has_value() && step_t->defined()) {
+    check_cuda_tensor(*step_t, "step_t");
+    TDSV_CHECK(step_t->scalar_type() == at::kInt, "adamw: step_t is an int32 device scalar");
+    stp = step_t->data_ptr<int>();
+  }
   if (n == 0) return;
   const float bc1 = static_cast<float>(1.0 - std::pow(beta1, static_cast<double>(step)));
   const float bc2s = static_cast<float>(std::sqrt(1.0 - std::pow(beta2, static_cast<double>(step))));
@@ -165,7 +178,7 @@ void adamw_step(at::Tensor& master, const at::Tensor& grad, at::Tensor& m, at::T
                                                    static_cast<float>(lr), static_cast<float>(beta1),         \
                                                    static_cast<float>(beta2), static_cast<float>(eps),        \
                                                    static_cast<float>(weight_decay), bc1, bc2s,               \
-                                                   static_cast<float>(grad_scale), gsp, vec)
+                                                   static_cast<float>(grad_scale), gsp, vec, stp)
   const bool g32 = grad.scalar_type() == at::kFloat;
   const bool m32 = m.scalar_type() == at::kFloat;
   auto gbf = reinterpret_cast<const __nv_bfloat16*>(grad.data_ptr());

@@ -93,6 +93,8 @@ struct PeerTables {
 
 struct OptimArgs {
   float lr, beta1, beta2, eps, decay, step_size, bc2_sqrt, grad_scale;
+  const int* step;       // device step count (bias corrections computed here) or null
+  const uint32_t* base;  // device epoch base added to the epoch argument, or null
 };
 
 // Steps 1-4 above for one unit. kAdam = false: SGD on the fp32 master (m, v unused).
@@ -103,6 +105,12 @@ __global__ void __launch_bounds__(kThreads) peer_update_kernel(
     const float* __restrict__ grad_scale_ptr, int* __restrict__ nonfinite, int* status, uint64_t limit_ns) {
   __shared__ int s_abort;
   if (threadIdx.x == 0) s_abort = 0;
+  if (a.base != nullptr) epoch += *reinterpret_cast<const volatile uint32_t*>(a.base);
+  if (kAdam && a.step != nullptr) {  // step count kept on the device (CUDA-graph replays)
+    const double st = static_cast<double>(*a.step);
+    a.step_size = static_cast<float>(a.lr / (1.0 - pow(static_cast<double>(a.beta1), st)));
+    a.bc2_sqrt = static_cast<float>(sqrt(1.0 - pow(static_cast<double>(a.beta2), st)));
+  }
   // 1. announce (every block stores the same value, so no block depends on another being
   //    resident), then every block waits for all ranks' announcements
   if (threadIdx.x < world) {
@@ -218,7 +226,8 @@ void peer_update(const at::Tensor& peer_grad, const at::Tensor& peer_param, cons
                  at::Tensor& master, const c10::optional<at::Tensor>& m, const c10::optional<at::Tensor>& v,
                  int64_t algo, double lr, double beta1, double beta2, double eps, double weight_decay, int64_t step,
                  double grad_scale, const c10::optional<at::Tensor>& grad_scale_t,
-                 const c10::optional<at::Tensor>& nonfinite, int64_t max_blocks) {
+                 const c10::optional<at::Tensor>& nonfinite, int64_t max_blocks,
+                 const c10::optional<at::Tensor>& step_t, const c10::optional<at::Tensor>& epoch_base) {
   check_cuda_tensor(master, "master");
   check_cuda_tensor(my_flags, "my_flags");
   const int world = static_cast<int>(peer_grad.numel());
@@ -235,13 +244,21 @@ void peer_update(const at::Tensor& peer_grad, const at::Tensor& peer_param, cons
   if (grad_scale_t.has_value() && grad_scale_t->defined()) gsp = grad_scale_t->data_ptr<float>();
   int* nf = nullptr;
   if (nonfinite.has_value() && nonfinite->defined()) nf = nonfinite->data_ptr<int>();
-  OptimArgs a{};
+  OptimArgs a{};  // NOLINT
   a.lr = static_cast<float>(lr);
   a.beta1 = static_cast<float>(beta1);
   a.beta2 = static_cast<float>(beta2);
   a.eps = static_cast<float>(eps);
   a.decay = static_cast<float>(1.0 - lr * weight_decay);
   a.grad_scale = static_cast<float>(grad_scale);
+  auto dev_scalar = [](const c10::optional<at::Tensor>& t, const char* name) -> const void* {
+    if (!t.has_value() || !t->defined()) return nullptr;
+    check_cuda_tensor(*t, name);
+    TDSV_CHECK(t->scalar_type() == at::kInt && t->numel() >= 1, name, ": int32 device scalar");
+    return t->data_ptr();
+  };
+  a.step = static_cast<const int*>(dev_scalar(step_t, "step_t"));
+  a.base = static_cast<const uint32_t*>(dev_scalar(epoch_base, "epoch_base"));
   if (algo == 0) {
     const double bc1 = 1.0 - std::pow(beta1, static_cast<double>(step));
     a.step_size = static_cast<float>(lr / bc1);

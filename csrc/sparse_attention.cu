@@ -74,7 +74,8 @@ struct SaSmem {
   float l_run[kHeadsCta];
   float alpha[kHeadsCta];
   int any_rescale;
-  int fail;  // a softmax warp's bounded wait gave up: the four warps leave together
+  int fail;   // a softmax warp's bounded wait gave up: the four warps leave together
+  int pfail;  // the same for the four producer warps
   uint32_t tmem_base;
 };
 
@@ -167,7 +168,10 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_fwd_kernel(const Sa
     tmem_alloc(&sm.tmem_base, Cfg::kTmemCols);
     tmem_relinquish();
   }
-  if (threadIdx.x == 0) sm.fail = 0;
+  if (threadIdx.x == 0) {
+    sm.fail = 0;
+    sm.pfail = 0;
+  }
   if (threadIdx.x < kHeadsCta) {
     const int h = hg * kHeadsCta + threadIdx.x;
     sm.m_run[threadIdx.x] = h < p.H ? p.sinks[h] * kLog2e : 0.f;
@@ -197,7 +201,10 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_fwd_kernel(const Sa
     }
     for (int it = 0; it < tiles; ++it) {
       const int buf = it % kBufs;
-      if (it >= kBufs && !warp_wait(&sm.k_empty[buf], ((it / kBufs) - 1) & 1, p.status, kSaWaitKEmpty)) {
+      // every producer warp waits, then the four agree before any named barrier below
+      if (it >= kBufs && !warp_wait(&sm.k_empty[buf], ((it / kBufs) - 1) & 1, p.status, kSaWaitKEmpty)) sm.pfail = 1;
+      producer_sync();
+      if (sm.pfail) {
         failed = true;
         break;
       }
@@ -424,6 +431,490 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_fwd_kernel(const Sa
   (void)failed;
 }
 
+// =============================================================================================
+// Backward
+// =============================================================================================
+// One CTA per (token, batch row, group of 64 heads), 288 threads, the same roles as the forward.
+// Per key tile (with P = exp2(S c - lse log2 e), Delta[h] = O[h] . dO[h], dS = P (dP - Delta)):
+//   S^T = K Q^T, dP^T = V dO^T        M = 128 keys, N = 64 heads, K = D       (TMEM [0,64), [64,128))
+//   dQ^T += K^T (scale dS^T)          M = 128 dims (D / 128 tiles), N = 64, K = 128 keys
+//   dKV[:, chunk] = P^T dO[:, chunk] + (scale dS^T) Q[:, chunk]
+//                                     M = 128 keys, N = 64 dims per chunk, K = 64 heads
+// P^T (bf16) goes to tensor memory as the A operand of dKV; scale dS^T (bf16) to shared memory,
+// where it is both the MN-major B operand of dQ^T and the K-major A operand of dKV. Key rows are
+// gathered D / 2 dims at a time: with D = 512 one half-buffer is resident and the first half is
+// gathered again for its dQ^T tiles (shared memory holds Q, dO, one half and dS^T); with D <= 256
+// both halves stay resident. The compute warps drain each dKV chunk from tensor memory and add it
+// to the fp32 gradient of its KV row with 16-byte vector reductions (the rows a tile shares with
+// other tokens meet there, as in the reference's default atomic path). dQ is written once per
+// (token, head) and the sink gradient partial -exp(sink - lse) Delta per (token, head).
+// TMEM: S [0,64), dP [64,128), dQ^T [128, 128 + 64 D/128), dKV chunk (64 cols), P^T (32 cols).
+//
+// Replaces _attention_backward_kernel of dsv41_train/models/dsv4/attention/sparse_attention.py:152-323.
+enum : int { kSbWaitQ = 521, kSbWaitK, kSbWaitKEmpty, kSbWaitS, kSbWaitSFree, kSbWaitDs, kSbWaitDsFree, kSbWaitDkv,
+             kSbWaitDkvFree, kSbWaitDq };
+
+template <int D>
+struct SbCfg {
+  static constexpr int kAtoms = D / 64;
+  static constexpr int kHalfAtoms = kAtoms / 2;          // atoms of one gathered half (D / 2 dims)
+  static constexpr int kBufs = D <= 256 ? 2 : 1;          // resident halves
+  static constexpr int kOTiles = D / 128;                 // dQ^T tiles
+  static constexpr int kChunks = D / 64;                  // dKV chunks of 64 dims
+  static constexpr uint32_t kColS = 0, kColDp = 64, kColDq = 128;
+  static constexpr uint32_t kColDkv = kColDq + kOTiles * 64;
+  static constexpr uint32_t kColP = kColDkv + 64;
+  static_assert(kColP + 32 <= 512, "tensor memory budget");
+};
+
+template <int D>
+struct SbSmem {
+  alignas(1024) uint8_t q[SbCfg<D>::kAtoms * kQAtom];
+  alignas(1024) uint8_t dout[SbCfg<D>::kAtoms * kQAtom];
+  alignas(1024) uint8_t k[SbCfg<D>::kBufs][SbCfg<D>::kHalfAtoms * kKAtom];  // contiguous halves
+  alignas(1024) uint8_t ds[kKeys * 128];
+  uint64_t qd_full;
+  uint64_t k_full[SbCfg<D>::kBufs];
+  uint64_t k_empty[SbCfg<D>::kBufs];
+  uint64_t s_full, s_free, ds_full, ds_free, dkv_full, dkv_free, dq_full;
+  const __nv_bfloat16* key_src[kKeys];
+  uint32_t key_ok[kKeys];
+  float lse2[kHeadsCta];
+  float delta[kHeadsCta];
+  float dpart[2][kHeadsCta];
+  int fail;   // compute warps leave together after a failed wait
+  int pfail;  // producer warps likewise
+  uint32_t tmem_base;
+};
+
+struct SbParams {
+  SaParams f;                     // inputs as in the forward (out / lse are read here)
+  const __nv_bfloat16* dout;      // [B, L, H, D]
+  __nv_bfloat16* dq;              // [B, L, H, D]
+  float* dkv;                     // [B, S, D] fp32, accumulated
+  float* dcomp;                   // [B, C, D] fp32, accumulated, or null
+  float* dsink_part;              // [B, L, H]
+  float scale;                    // D^-1/2
+  // ordered (deterministic) mode: per-edge dKV rows [B, chunk, W + K, groups, D] fp32 instead of
+  // reductions; the CTAs cover tokens [t0, t0 + chunk) and ordered_edge_reduce sums the edges
+  float* edges;
+  int t0, chunk;
+};
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+template <int D>
+__global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_bwd_kernel(const SbParams sp) {
+  using Cfg = SbCfg<D>;
+  constexpr int kBufs = Cfg::kBufs;
+  constexpr int kLoadsPerTile = kBufs == 1 ? 3 : 2;  // D = 512: half 0, half 1, half 0 again
+  const SaParams& p = sp.f;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  SbSmem<D>& sm = *reinterpret_cast<SbSmem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int t = sp.t0 + blockIdx.x, b = blockIdx.y, hg = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tiles = (p.W + p.K + kKeys - 1) / kKeys;
+  const int64_t tok = static_cast<int64_t>(b) * p.L + t;
+  const int heads_here = min(kHeadsCta, p.H - hg * kHeadsCta);
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.qd_full, 128);
+    for (int i = 0; i < kBufs; ++i) {
+      mbar_init(&sm.k_full[i], 128);
+      mbar_init(&sm.k_empty[i], 1);
+    }
+    mbar_init(&sm.s_full, 1);
+    mbar_init(&sm.s_free, 128);
+    mbar_init(&sm.ds_full, 128);
+    mbar_init(&sm.ds_free, 1);
+    mbar_init(&sm.dkv_full, 1);
+    mbar_init(&sm.dkv_free, 128);
+    mbar_init(&sm.dq_full, 1);
+    fence_barrier_init();
+    sm.fail = 0;
+    sm.pfail = 0;
+  }
+  if (warp == 4) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  // which half a load carries, and into which buffer
+  auto load_half = [&](int n) { return kBufs == 1 ? ((n % 3) == 1 ? 1 : 0) : (n % 2); };
+  auto load_buf = [&](int n) { return kBufs == 1 ? 0 : (n % 2); };
+  auto load_use = [&](int n) { return kBufs == 1 ? n : n / 2; };  // earlier loads into the same buffer
+
+  if (warp >= 5) {
+    // ---------------- gather producers ----------------
+    const int pt = threadIdx.x - 160;
+    {
+      const __nv_bfloat16* qsrc = p.q + (tok * p.H + hg * kHeadsCta) * D;
+      const __nv_bfloat16* dsrc = sp.dout + (tok * p.H + hg * kHeadsCta) * D;
+      const uint32_t qb = smem_u32(sm.q), db = smem_u32(sm.dout);
+      for (int c = pt; c < kHeadsCta * (D / 8); c += 128) {
+        const int row = c / (D / 8), ch = c % (D / 8);
+        const bool ok = row < heads_here;
+        const uint32_t off = (ch >> 3) * kQAtom + swz(row, ch & 7);
+        cp_async16(qb + off, qsrc + (ok ? row * D + ch * 8 : 0), ok);
+        cp_async16(db + off, dsrc + (ok ? row * D + ch * 8 : 0), ok);
+      }
+      cp_async_commit();
+      cp_async_wait_all();
+      fence_proxy_async_smem();
+      mbar_arrive(&sm.qd_full);
+    }
+    for (int it = 0; it < tiles; ++it) {
+      {
+        bool ok;
+        sm.key_src[pt] = key_row<D>(p, b, t, it * kKeys + pt, ok);
+        sm.key_ok[pt] = ok ? 1u : 0u;
+      }
+      producer_sync();
+      for (int j = 0; j < kLoadsPerTile; ++j) {
+        const int n = it * kLoadsPerTile + j;
+        const int buf = load_buf(n), half = load_half(n), use = load_use(n);
+        if (use >= 1 && !warp_wait(&sm.k_empty[buf], (use - 1) & 1, p.status, kSbWaitKEmpty)) sm.pfail = 1;
+        producer_sync();
+        if (sm.pfail) break;
+        const uint32_t kb = smem_u32(sm.k[buf]);
+        constexpr int kHalfChunks = D / 16;  // 16-byte chunks per half row
+        for (int c = pt; c < kKeys * kHalfChunks; c += 128) {
+          const int row = c / kHalfChunks, ch = c % kHalfChunks;
+          cp_async16(kb + (ch >> 3) * kKAtom + swz(row, ch & 7), sm.key_src[row] + half * (D / 2) + ch * 8,
+                     sm.key_ok[row] != 0);
+        }
+        cp_async_commit();
+        cp_async_wait_all();
+        fence_proxy_async_smem();
+        mbar_arrive(&sm.k_full[buf]);
+      }
+      producer_sync();
+      if (sm.pfail) break;
+    }
+  } else if (warp == 4) {
+    // ---------------- MMA issuer ----------------
+    const bool leader = elect_one();
+    const uint32_t idesc_sdp = make_idesc_bf16(kKeys, kHeadsCta, false, false);
+    const uint32_t idesc_dq = make_idesc_bf16(128, kHeadsCta, true, true);
+    const uint32_t idesc_dkv = make_idesc_bf16(kKeys, 64, false, true);
+    const uint32_t qb = smem_u32(sm.q), db = smem_u32(sm.dout), dsb = smem_u32(sm.ds);
+    bool ok = warp_wait(&sm.qd_full, 0, p.status, kSbWaitQ);
+    auto wait_load = [&](int n) {
+      return warp_wait(&sm.k_full[load_buf(n)], load_use(n) & 1, p.status, kSbWaitK);
+    };
+    // S^T and dP^T over the dims of one gathered half
+    auto issue_sdp = [&](int n, bool first) {
+      const int half = load_half(n);
+      const uint32_t kb = smem_u32(sm.k[load_buf(n)]);
+      if (leader) {
+#pragma unroll 4
+        for (int kk = 0; kk < D / 32; ++kk) {
+          const uint64_t a = kmajor_desc(kb, kk, kKAtom);
+          const int gk = half * (D / 32) + kk;  // k-step in the full head dim
+          umma_f16(tmem + Cfg::kColS, a, kmajor_desc(qb, gk, kQAtom), idesc_sdp, (first && kk == 0) ? 0u : 1u);
+          umma_f16(tmem + Cfg::kColDp, a, kmajor_desc(db, gk, kQAtom), idesc_sdp, (first && kk == 0) ? 0u : 1u);
+        }
+      }
+    };
+    // dQ^T tiles whose dims lie in the resident half(s)
+    auto issue_dq = [&](int n, int m_lo, int m_hi, bool first_tile) {
+      const uint32_t kb0 = smem_u32(sm.k[0]);
+      if (leader) {
+        for (int m = m_lo; m < m_hi; ++m) {
+          // atom of dims [128 m, 128 m + 64): with one buffer it is relative to the resident half
+          const int atom = kBufs == 1 ? 2 * m - load_half(n) * Cfg::kHalfAtoms : 2 * m;
+#pragma unroll
+          for (int kk = 0; kk < kKeys / 16; ++kk) {
+            umma_f16(tmem + Cfg::kColDq + m * 64, mnmajor_desc(kb0 + atom * kKAtom, kk, kKAtom),
+                     mnmajor_desc(dsb, kk, kKeys * 128), idesc_dq, (first_tile && kk == 0) ? 0u : 1u);
+          }
+        }
+      }
+    };
+    int g = 0;  // dKV chunk counter
+    for (int it = 0; ok && it < tiles; ++it) {
+      const int n0 = it * kLoadsPerTile;
+      if (it > 0 && !warp_wait(&sm.s_free, (it - 1) & 1, p.status, kSbWaitSFree)) { ok = false; break; }
+      // S^T, dP^T: half 0 then half 1
+      if (!wait_load(n0)) { ok = false; break; }
+      tc_fence_after();
+      issue_sdp(n0, true);
+      if (kBufs == 1 && leader) umma_commit(&sm.k_empty[0]);
+      __syncwarp();
+      if (!wait_load(n0 + 1)) { ok = false; break; }
+      tc_fence_after();
+      issue_sdp(n0 + 1, false);
+      if (leader) umma_commit(&sm.s_full);
+      __syncwarp();
+      // P^T (TMEM) and dS^T (shared) are ready
+      if (!warp_wait(&sm.ds_full, it & 1, p.status, kSbWaitDs)) { ok = false; break; }
+      tc_fence_after();
+      if (kBufs == 1) {
+        issue_dq(n0 + 1, Cfg::kOTiles / 2, Cfg::kOTiles, it == 0);  // tiles of the resident half 1
+        if (leader) umma_commit(&sm.k_empty[0]);
+      } else {
+        issue_dq(n0 + 1, 0, Cfg::kOTiles, it == 0);                 // both halves resident
+        if (leader) {
+          umma_commit(&sm.k_empty[0]);
+          umma_commit(&sm.k_empty[1]);
+        }
+      }
+      __syncwarp();
+      // dKV chunks of 64 dims
+      for (int c = 0; c < Cfg::kChunks; ++c, ++g) {
+        if (g > 0 && !warp_wait(&sm.dkv_free, (g - 1) & 1, p.status, kSbWaitDkvFree)) { ok = false; break; }
+        tc_fence_after();
+        if (leader) {
+          const uint32_t bq = qb + c * kQAtom, bd = db + c * kQAtom;
+#pragma unroll
+          for (int kk = 0; kk < kHeadsCta / 16; ++kk) {
+            umma_f16_ts(tmem + Cfg::kColDkv, tmem + Cfg::kColP + kk * 8, mnmajor_desc(bd, kk, kQAtom), idesc_dkv,
+                        kk > 0 ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < kHeadsCta / 16; ++kk) {
+            umma_f16(tmem + Cfg::kColDkv, kmajor_desc(dsb, kk, kKeys * 128), mnmajor_desc(bq, kk, kQAtom), idesc_dkv,
+                     1u);
+          }
+          umma_commit(&sm.dkv_full);
+          if (c == Cfg::kChunks - 1) umma_commit(&sm.ds_free);
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+      if (kBufs == 1) {  // half 0 again for its dQ^T tiles
+        if (!wait_load(n0 + 2)) { ok = false; break; }
+        tc_fence_after();
+        issue_dq(n0 + 2, 0, Cfg::kOTiles / 2, it == 0);
+        if (leader) umma_commit(&sm.k_empty[0]);
+        __syncwarp();
+      }
+    }
+    if (ok && leader) umma_commit(&sm.dq_full);
+    __syncwarp();
+  } else {
+    // ---------------- compute warps 0-3 (thread = key row = TMEM lane) ----------------
+    const int row = threadIdx.x;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    // Delta[h] = O[h] . dO[h] (two threads per head), lse in the exp2 domain, sink-gradient partial
+    {
+      const int h = row >> 1, part = row & 1;
+      float acc = 0.f;
+      if (h < heads_here) {
+        const __nv_bfloat16* o = p.out + (tok * p.H + hg * kHeadsCta + h) * D + part * (D / 2);
+        const __nv_bfloat16* g = sp.dout + (tok * p.H + hg * kHeadsCta + h) * D + part * (D / 2);
+        for (int d = 0; d < D / 2; d += 8) {
+          float a[8], c[8];
+          load_bf16x8(o + d, a);
+          load_bf16x8(g + d, c);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc += a[q] * c[q];
+        }
+      }
+      sm.dpart[part][h] = acc;
+      softmax_sync();
+      if (row < kHeadsCta) {
+        const float dlt = sm.dpart[0][row] + sm.dpart[1][row];
+        sm.delta[row] = dlt;
+        if (row < heads_here) {
+          const int64_t hi = tok * p.H + hg * kHeadsCta + row;
+          const float l = p.lse[hi];
+          sm.lse2[row] = l * kLog2e;
+          sp.dsink_part[hi] = -__expf(p.sinks[hg * kHeadsCta + row] - l) * dlt;
+        } else {
+          sm.lse2[row] = 0.f;
+        }
+      }
+      softmax_sync();
+    }
+    bool failed = false;
+    int g = 0;
+    for (int it = 0; it < tiles && !failed; ++it) {
+      if (!warp_wait(&sm.s_full, it & 1, p.status, kSbWaitS)) sm.fail = 1;
+      softmax_sync();
+      if (sm.fail) break;
+      tc_fence_after();
+      float sv[64], dp[64];
+      {
+        uint32_t r[32];
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          tmem_ld_32x32b_x32(lane_base + Cfg::kColS + hh * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sv[hh * 32 + j] = __uint_as_float(r[j]);
+          tmem_ld_32x32b_x32(lane_base + Cfg::kColDp + hh * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) dp[hh * 32 + j] = __uint_as_float(r[j]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&sm.s_free);
+      bool valid;
+      const __nv_bfloat16* src = key_row<D>(p, b, t, it * kKeys + row, valid);
+      // P and scale * dS
+      uint32_t pk[32];
+#pragma unroll
+      for (int j = 0; j < 64; j += 2) {
+        float p0 = valid && j < heads_here ? ex2_approx(sv[j] * p.scale_log2 - sm.lse2[j]) : 0.f;
+        float p1 = valid && j + 1 < heads_here ? ex2_approx(sv[j + 1] * p.scale_log2 - sm.lse2[j + 1]) : 0.f;
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+        pk[j / 2] = *reinterpret_cast<uint32_t*>(&h2);
+        dp[j] = p0 * (dp[j] - sm.delta[j]) * sp.scale;
+        dp[j + 1] = p1 * (dp[j + 1] - sm.delta[j + 1]) * sp.scale;
+      }
+      if (it > 0 && !warp_wait(&sm.ds_free, (it - 1) & 1, p.status, kSbWaitDsFree)) sm.fail = 1;
+      softmax_sync();
+      if (sm.fail) break;
+      tc_fence_after();
+      tmem_st_32x32b_x32(lane_base + Cfg::kColP, pk);
+      {
+        uint8_t* drow = sm.ds + row * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 w;
+          uint32_t* wp = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(dp[8 * c + 2 * q], dp[8 * c + 2 * q + 1]);
+            wp[q] = *reinterpret_cast<uint32_t*>(&h2);
+          }
+          *reinterpret_cast<uint4*>(drow + ((c ^ (row & 7)) << 4)) = w;
+        }
+      }
+      tmem_st_wait();
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(&sm.ds_full);
+      // drain the dKV chunks into the fp32 gradient of this key's row
+      const int j = it * kKeys + row;
+      float* dst = nullptr;
+      const bool ordered = sp.edges != nullptr;
+      if (valid) {
+        if (ordered) {  // this (token, entry, head group)'s own edge row: plain stores
+          dst = sp.edges + (((static_cast<int64_t>(b) * sp.chunk + (t - sp.t0)) * (p.W + p.K) + j) * gridDim.z + hg) * D;
+        } else if (j < p.W) {
+          dst = sp.dkv + (src - p.kv);
+        } else {
+          dst = sp.dcomp + (src - p.comp);
+        }
+      }
+      for (int c = 0; c < Cfg::kChunks; ++c, ++g) {
+        if (!warp_wait(&sm.dkv_full, g & 1, p.status, kSbWaitDkv)) sm.fail = 1;
+        softmax_sync();
+        if (sm.fail) {
+          failed = true;
+          break;
+        }
+        tc_fence_after();
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(lane_base + Cfg::kColDkv + hh * 32, r);
+          tmem_ld_wait();
+          if (dst != nullptr && ordered) {
+#pragma unroll
+            for (int q = 0; q < 32; q += 4) {
+              *reinterpret_cast<float4*>(dst + c * 64 + hh * 32 + q) =
+                  make_float4(__uint_as_float(r[q]), __uint_as_float(r[q + 1]), __uint_as_float(r[q + 2]),
+                              __uint_as_float(r[q + 3]));
+            }
+          } else if (dst != nullptr) {
+#pragma unroll
+            for (int q = 0; q < 32; q += 4) {
+              red_add_v4(dst + c * 64 + hh * 32 + q, __uint_as_float(r[q]), __uint_as_float(r[q + 1]),
+                         __uint_as_float(r[q + 2]), __uint_as_float(r[q + 3]));
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&sm.dkv_free);
+      }
+    }
+    if (!failed && !sm.fail && !warp_wait(&sm.dq_full, 0, p.status, kSbWaitDq)) sm.fail = 1;
+    softmax_sync();
+    if (!sm.fail) {
+      tc_fence_after();
+      // dQ staged as bf16 [64 heads x D] over the idle key buffer(s), then one contiguous store
+      __nv_bfloat16* stage = reinterpret_cast<__nv_bfloat16*>(sm.k[0]);
+#pragma unroll 1
+      for (int m = 0; m < Cfg::kOTiles; ++m) {
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(lane_base + Cfg::kColDq + m * 64 + hh * 32, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < 32; ++q) stage[(hh * 32 + q) * D + m * 128 + row] = __float2bfloat16_rn(__uint_as_float(r[q]));
+        }
+      }
+      softmax_sync();
+      const uint4* from = reinterpret_cast<const uint4*>(stage);
+      uint4* to = reinterpret_cast<uint4*>(sp.dq + (tok * p.H + hg * kHeadsCta) * D);
+      for (int i = row; i < heads_here * D / 8; i += 128) to[i] = from[i];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int D>
+void launch_bwd(const SbParams& prm, int tokens, int B, int groups) {
+  const size_t smem = sizeof(SbSmem<D>) + 1024;
+  static bool configured = false;
+  if (!configured) {
+    TDSV_CUDA_CHECK(cudaFuncSetAttribute(sparse_attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(smem)));
+    configured = true;
+  }
+  sparse_attn_bwd_kernel<D><<<dim3(tokens, B, groups), kSaThreads, smem, stream()>>>(prm);
+}
+
+// Deterministic sum of per-edge dKV rows: one CTA per destination row r (window rows first, then
+// compressed rows), its edges in `order[offsets[r] .. offsets[r + 1])` (ascending edge id, the
+// stable sort of the chunk's destinations) and, within an edge, the head groups in order. The sum
+// is added to the row's fp32 gradient by its only writer.
+__global__ void ordered_edge_reduce_kernel(const float* __restrict__ edges, const int64_t* __restrict__ order,
+                                           const int64_t* __restrict__ offsets, float* __restrict__ dkv,
+                                           float* __restrict__ dcomp, int64_t kv_rows, int groups, int D) {
+  const int64_t r = blockIdx.x;
+  const int64_t lo = offsets[r], hi = offsets[r + 1];
+  if (lo == hi) return;
+  float* out = r < kv_rows ? dkv + r * D : dcomp + (r - kv_rows) * D;
+  for (int d = threadIdx.x * 4; d < D; d += blockDim.x * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t e = lo; e < hi; ++e) {
+      const float* row = edges + order[e] * groups * D + d;
+      for (int g = 0; g < groups; ++g) {
+        const float4 v = *reinterpret_cast<const float4*>(row + g * D);
+        acc.x += v.x;
+        acc.y += v.y;
+        acc.z += v.z;
+        acc.w += v.w;
+      }
+    }
+    float4 cur = *reinterpret_cast<float4*>(out + d);
+    cur.x += acc.x;
+    cur.y += acc.y;
+    cur.z += acc.z;
+    cur.w += acc.w;
+    *reinterpret_cast<float4*>(out + d) = cur;
+  }
+}
+
 template <int D>
 void launch_fwd(const SaParams& prm, int L, int B, int groups) {
   const size_t smem = sizeof(SaSmem<D>) + 1024;
@@ -438,26 +929,28 @@ void launch_fwd(const SaParams& prm, int L, int B, int groups) {
 
 }  // namespace
 
-// out [B, L, H, D] bf16, lse [B, L, H] fp32.
-std::vector<at::Tensor> sparse_attention_fwd(const at::Tensor& q, const at::Tensor& kv, const at::Tensor& win_idx,
-                                             const at::Tensor& win_mask, const c10::optional<at::Tensor>& comp,
-                                             const c10::optional<at::Tensor>& comp_idx, const at::Tensor& sinks) {
+namespace {
+
+// Shared argument checks of the forward and backward entry points.
+SaParams make_params(const at::Tensor& q, const at::Tensor& kv, const at::Tensor& win_idx, const at::Tensor& win_mask,
+                     const c10::optional<at::Tensor>& comp, const c10::optional<at::Tensor>& comp_idx,
+                     const at::Tensor& sinks) {
   check_cuda_tensor(q, "q");
   check_cuda_tensor(kv, "kv");
   check_cuda_tensor(win_idx, "window_indices");
   check_cuda_tensor(win_mask, "window_mask");
   check_cuda_tensor(sinks, "sinks");
-  TDSV_CHECK(q.dim() == 4 && kv.dim() == 3, "sparse_attention_fwd: q [B, L, H, D], kv [B, S, D]");
+  TDSV_CHECK(q.dim() == 4 && kv.dim() == 3, "sparse_attention: q [B, L, H, D], kv [B, S, D]");
   const int B = static_cast<int>(q.size(0)), L = static_cast<int>(q.size(1)), H = static_cast<int>(q.size(2));
   const int D = static_cast<int>(q.size(3));
-  TDSV_CHECK(q.scalar_type() == at::kBFloat16 && kv.scalar_type() == at::kBFloat16, "sparse_attention_fwd: bf16");
-  TDSV_CHECK(D == 128 || D == 256 || D == 512, "sparse_attention_fwd: head dim 128, 256 or 512");
-  TDSV_CHECK(kv.size(0) == B && kv.size(2) == D, "sparse_attention_fwd: kv shape");
+  TDSV_CHECK(q.scalar_type() == at::kBFloat16 && kv.scalar_type() == at::kBFloat16, "sparse_attention: bf16");
+  TDSV_CHECK(D == 128 || D == 256 || D == 512, "sparse_attention: head dim 128, 256 or 512");
+  TDSV_CHECK(kv.size(0) == B && kv.size(2) == D, "sparse_attention: kv shape");
   TDSV_CHECK(win_idx.scalar_type() == at::kLong && win_idx.dim() == 3 && win_idx.size(0) == B && win_idx.size(1) == L,
-             "sparse_attention_fwd: window_indices int64 [B, L, W]");
+             "sparse_attention: window_indices int64 [B, L, W]");
   TDSV_CHECK(win_mask.scalar_type() == at::kBool && win_mask.sizes() == win_idx.sizes(),
-             "sparse_attention_fwd: window_mask bool [B, L, W]");
-  TDSV_CHECK(sinks.scalar_type() == at::kFloat && sinks.numel() == H, "sparse_attention_fwd: sinks fp32 [H]");
+             "sparse_attention: window_mask bool [B, L, W]");
+  TDSV_CHECK(sinks.scalar_type() == at::kFloat && sinks.numel() == H, "sparse_attention: sinks fp32 [H]");
   SaParams prm{};
   prm.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
   prm.kv = reinterpret_cast<const __nv_bfloat16*>(kv.data_ptr());
@@ -468,24 +961,34 @@ std::vector<at::Tensor> sparse_attention_fwd(const at::Tensor& q, const at::Tens
   prm.H = H;
   prm.S = static_cast<int>(kv.size(1));
   prm.W = static_cast<int>(win_idx.size(2));
-  prm.K = 0;
-  prm.C = 0;
   if (comp.has_value() && comp->defined() && comp_idx.has_value() && comp_idx->defined()) {
     check_cuda_tensor(*comp, "compressed_kv");
     check_cuda_tensor(*comp_idx, "compressed_indices");
     TDSV_CHECK(comp->scalar_type() == at::kBFloat16 && comp->dim() == 3 && comp->size(0) == B && comp->size(2) == D,
-               "sparse_attention_fwd: compressed_kv bf16 [B, C, D]");
+               "sparse_attention: compressed_kv bf16 [B, C, D]");
     TDSV_CHECK(comp_idx->scalar_type() == at::kLong && comp_idx->dim() == 3 && comp_idx->size(0) == B &&
                    comp_idx->size(1) == L,
-               "sparse_attention_fwd: compressed_indices int64 [B, L, K]");
+               "sparse_attention: compressed_indices int64 [B, L, K]");
     prm.comp = reinterpret_cast<const __nv_bfloat16*>(comp->data_ptr());
     prm.comp_idx = comp_idx->data_ptr<int64_t>();
     prm.C = static_cast<int>(comp->size(1));
     prm.K = static_cast<int>(comp_idx->size(2));
   }
-  TDSV_CHECK(prm.W + prm.K > 0, "sparse_attention_fwd: no keys");
+  TDSV_CHECK(prm.W + prm.K > 0, "sparse_attention: no keys");
   prm.scale_log2 = static_cast<float>(std::pow(static_cast<double>(D), -0.5)) * kLog2e;
   prm.status = status_word_ptr();
+  return prm;
+}
+
+}  // namespace
+
+// out [B, L, H, D] bf16, lse [B, L, H] fp32 (natural log, sink included).
+std::vector<at::Tensor> sparse_attention_fwd(const at::Tensor& q, const at::Tensor& kv, const at::Tensor& win_idx,
+                                             const at::Tensor& win_mask, const c10::optional<at::Tensor>& comp,
+                                             const c10::optional<at::Tensor>& comp_idx, const at::Tensor& sinks) {
+  SaParams prm = make_params(q, kv, win_idx, win_mask, comp, comp_idx, sinks);
+  const int B = static_cast<int>(q.size(0)), L = static_cast<int>(q.size(1)), H = static_cast<int>(q.size(2));
+  const int D = static_cast<int>(q.size(3));
   auto out = at::empty({B, L, H, D}, q.options());
   auto lse = at::empty({B, L, H}, q.options().dtype(at::kFloat));
   prm.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
@@ -498,6 +1001,93 @@ std::vector<at::Tensor> sparse_attention_fwd(const at::Tensor& q, const at::Tens
   else launch_fwd<512>(prm, L, B, groups);
   TDSV_LAUNCH_CHECK();
   return {out, lse};
+}
+
+// dq [B, L, H, D] bf16, dkv [B, S, D] fp32, dcompressed [B, C, D] fp32 (empty without compressed
+// keys), dsink partials [B, L, H] fp32 (sum over B and L for the sink gradient).
+std::vector<at::Tensor> sparse_attention_bwd(const at::Tensor& q, const at::Tensor& kv, const at::Tensor& win_idx,
+                                             const at::Tensor& win_mask, const c10::optional<at::Tensor>& comp,
+                                             const c10::optional<at::Tensor>& comp_idx, const at::Tensor& sinks,
+                                             const at::Tensor& out, const at::Tensor& lse, const at::Tensor& dout,
+                                             c10::optional<int64_t> ordered_chunk) {
+  SbParams sp{};
+  sp.f = make_params(q, kv, win_idx, win_mask, comp, comp_idx, sinks);
+  check_cuda_tensor(out, "out");
+  check_cuda_tensor(lse, "lse");
+  check_cuda_tensor(dout, "dout");
+  TDSV_CHECK(out.sizes() == q.sizes() && dout.sizes() == q.sizes() && dout.scalar_type() == at::kBFloat16 &&
+                 out.scalar_type() == at::kBFloat16,
+             "sparse_attention_bwd: out / dout bf16 like q");
+  const int B = static_cast<int>(q.size(0)), L = static_cast<int>(q.size(1)), H = static_cast<int>(q.size(2));
+  const int D = static_cast<int>(q.size(3));
+  TDSV_CHECK(lse.scalar_type() == at::kFloat && lse.numel() == static_cast<int64_t>(B) * L * H,
+             "sparse_attention_bwd: lse fp32 [B, L, H]");
+  sp.f.out = const_cast<__nv_bfloat16*>(reinterpret_cast<const __nv_bfloat16*>(out.data_ptr()));
+  sp.f.lse = const_cast<float*>(lse.data_ptr<float>());
+  sp.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  auto dq = at::empty_like(q);
+  auto dkv = at::zeros(kv.sizes(), kv.options().dtype(at::kFloat));
+  at::Tensor dcomp;
+  if (sp.f.comp != nullptr) {
+    dcomp = at::zeros(comp->sizes(), comp->options().dtype(at::kFloat));
+    sp.dcomp = dcomp.data_ptr<float>();
+  }
+  auto dsink = at::empty({B, L, H}, q.options().dtype(at::kFloat));
+  sp.dq = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
+  sp.dkv = dkv.data_ptr<float>();
+  sp.dsink_part = dsink.data_ptr<float>();
+  sp.scale = static_cast<float>(std::pow(static_cast<double>(D), -0.5));
+  sp.chunk = L;
+  if (B * L == 0) return {dq, dkv, dcomp, dsink};
+  c10::cuda::CUDAGuard guard(q.device());
+  const int groups = (H + kHeadsCta - 1) / kHeadsCta;
+  if (!ordered_chunk.has_value()) {
+    if (D == 128) launch_bwd<128>(sp, L, B, groups);
+    else if (D == 256) launch_bwd<256>(sp, L, B, groups);
+    else launch_bwd<512>(sp, L, B, groups);
+    TDSV_LAUNCH_CHECK();
+    return {dq, dkv, dcomp, dsink};
+  }
+  // Deterministic KV gradients: token chunks in order; per chunk, every (token, entry, head group)
+  // stores its own dKV row, then each destination row sums its edges in ascending edge order.
+  const int chunk = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(*ordered_chunk, L)));
+  const int slots = sp.f.W + sp.f.K;
+  const int64_t kv_rows = static_cast<int64_t>(B) * sp.f.S;
+  const int64_t rows = kv_rows + static_cast<int64_t>(B) * sp.f.C;
+  auto edges = at::empty({B, chunk, slots, groups, D}, q.options().dtype(at::kFloat));
+  sp.edges = edges.data_ptr<float>();
+  sp.chunk = chunk;
+  // destination row of every edge of the whole sequence (rows = invalid)
+  auto opts = win_idx.options();
+  auto wvalid = win_mask & (win_idx >= 0) & (win_idx < sp.f.S);
+  auto batch_kv = at::arange(B, opts).view({B, 1, 1}) * sp.f.S;
+  auto wdest = at::where(wvalid, win_idx + batch_kv, at::full({}, rows, opts));
+  at::Tensor dest = wdest;
+  if (sp.f.K > 0) {
+    auto cvalid = (*comp_idx >= 0) & (*comp_idx < sp.f.C);
+    auto batch_c = at::arange(B, opts).view({B, 1, 1}) * sp.f.C + kv_rows;
+    dest = at::cat({wdest, at::where(cvalid, *comp_idx + batch_c, at::full({}, rows, opts))}, 2);
+  }
+  for (int t0 = 0; t0 < L; t0 += chunk) {
+    const int n = std::min(chunk, L - t0);
+    sp.t0 = t0;
+    if (D == 128) launch_bwd<128>(sp, n, B, groups);
+    else if (D == 256) launch_bwd<256>(sp, n, B, groups);
+    else launch_bwd<512>(sp, n, B, groups);
+    TDSV_LAUNCH_CHECK();
+    // edge ids local to the chunk buffer: (b * chunk + (t - t0)) * slots + j
+    auto d = dest.narrow(1, t0, n);                                       // [B, n, slots]
+    if (n < chunk) d = at::cat({d, at::full({B, chunk - n, slots}, rows, opts)}, 1);
+    auto flat = d.reshape({-1});
+    auto order = std::get<1>(at::sort(flat, /*stable=*/true, /*dim=*/0, /*descending=*/false));
+    auto counts = at::bincount(flat, /*weights=*/{}, rows + 1).narrow(0, 0, rows);
+    auto offsets = at::cat({at::zeros({1}, counts.options()), counts.cumsum(0)});
+    ordered_edge_reduce_kernel<<<static_cast<unsigned>(rows), 128, 0, stream()>>>(
+        edges.data_ptr<float>(), order.data_ptr<int64_t>(), offsets.data_ptr<int64_t>(), dkv.data_ptr<float>(),
+        sp.f.C > 0 ? dcomp.data_ptr<float>() : nullptr, kv_rows, groups, D);
+    TDSV_LAUNCH_CHECK();
+  }
+  return {dq, dkv, dcomp, dsink};
 }
 
 }  // namespace tdsv

@@ -166,7 +166,10 @@ class Qwen3MoeSparseMoeBlock(nn.Module):
         if self.stats is not None:
             with torch.no_grad():
                 probs = torch.softmax(router_logits.float(), dim=-1)
-                counts = torch.bincount(selected.reshape(-1).long(), minlength=self.num_experts)
+                # scatter-add instead of bincount, which reads the maximum back to the host
+                ids = selected.reshape(-1).long()
+                counts = torch.zeros(self.num_experts, dtype=torch.long, device=ids.device).scatter_add_(
+                    0, ids, torch.ones_like(ids))
                 self.stats.append((counts.float(), probs.sum(0), probs.shape[0]))
         out = self.experts(flat, selected, weights)
         return out.reshape(batch, length, size), router_logits
@@ -230,8 +233,10 @@ class Qwen3MoeModel(nn.Module):
             if cache is not None:
                 hidden, logits = layer(hidden, position_ids, attention_mask, cache)
             elif self.gradient_checkpointing and self.training and torch.is_grad_enabled():
+                # the RNG state matters only with dropout (and reading it is not allowed in a CUDA-graph capture)
                 hidden, logits = checkpoint(layer, hidden, position_ids, attention_mask, use_reentrant=False,
-                                            context_fn=replay.checkpoint_contexts)
+                                            context_fn=replay.checkpoint_contexts,
+                                            preserve_rng_state=self.config.attention_dropout > 0)
             else:
                 hidden, logits = layer(hidden, position_ids, attention_mask)
             if output_router_logits and logits is not None:
@@ -317,7 +322,7 @@ class Qwen3MoeForCausalLM(nn.Module):
         experts = self.config.num_experts
         counts = torch.stack([c for c, _, _ in stats]).sum(0)
         psum = torch.stack([p for _, p, _ in stats]).sum(0)
-        total = torch.tensor(float(sum(n for _, _, n in stats)), device=counts.device)
+        total = counts.new_full((), float(sum(n for _, _, n in stats)), dtype=torch.float32)  # no host copy
         cp = self.context_parallel
         counts, psum, total = cp.sum(counts), cp.sum(psum), cp.sum(total)
         aux = experts * ((counts / total) * (psum / total)).sum()

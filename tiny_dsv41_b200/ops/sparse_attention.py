@@ -14,9 +14,10 @@ On CUDA, ``index_scores`` runs the tcgen05 kernel of ``csrc/index_scores.cu`` (k
 operand, the block's (query, head) rows as N, relu / head weights / head reduction in the TMEM
 epilogue; head dim 64 or 128, heads a power of two from 4 to 64). ``sparse_attention`` runs the
 tcgen05 forward of ``csrc/sparse_attention.cu`` (gathered keys as the M operand, 64 heads as N,
-online softmax seeded with the sink; bf16, head dim 128 / 256 / 512, no dropout); its backward
-recomputes the gathered restatement below in fp32 under autograd. Other shapes run the
-restatement itself, which is also the oracle on CPU.
+online softmax seeded with the sink; bf16, head dim 128 / 256 / 512, no dropout) and its tcgen05
+backward (dQ per token, dKV rows added with fp32 vector reductions, or with
+``deterministic=True`` per-edge rows summed in a fixed order by an owner per KV row). Other shapes
+run the restatement below, which is also the oracle on CPU.
 """
 
 from __future__ import annotations
@@ -36,39 +37,52 @@ def _sparse_kernel_ok(query, kv, window_indices, compressed_kv, compressed_indic
 
 
 class _SparseAttention(torch.autograd.Function):
-    """Kernel forward; backward by recomputing the gathered restatement under autograd."""
+    """tcgen05 forward and backward (``csrc/sparse_attention.cu``). The backward adds the KV
+    gradients of rows shared by several tokens with fp32 vector reductions; ``deterministic``
+    stores every (token, entry) edge's KV gradient row instead and sums each KV row over its edges
+    in ascending edge order, chunk by chunk (the ordered-dKV scheme of the reference's
+    ``ordered_kv.py``), so repeated runs are bitwise equal."""
 
     @staticmethod
-    def forward(ctx, query, kv, window_indices, window_mask, compressed_kv, compressed_indices, sinks):
+    def forward(ctx, query, kv, window_indices, window_mask, compressed_kv, compressed_indices, sinks, deterministic):
         q = query.transpose(1, 2).contiguous()  # [B, L, H, D]: free when the projection wrote it that way
+        kv_c = kv.contiguous()
+        widx = window_indices.long().contiguous()
+        wmask = window_mask.bool().contiguous()
         comp = None if compressed_kv is None else compressed_kv.contiguous()
         cidx = None if compressed_indices is None else compressed_indices.long().contiguous()
-        out, lse = ext().sparse_attention_fwd(q, kv.contiguous(), window_indices.long().contiguous(),
-                                              window_mask.bool().contiguous(), comp, cidx,
-                                              sinks.float().contiguous())
-        ctx.save_for_backward(query, kv, window_indices, window_mask, compressed_kv, compressed_indices, sinks)
+        sk = sinks.float().contiguous()
+        out, lse = ext().sparse_attention_fwd(q, kv_c, widx, wmask, comp, cidx, sk)
+        ctx.deterministic = deterministic
+        ctx.has_comp = comp is not None
+        ctx.sinks_dtype = sinks.dtype
+        ctx.save_for_backward(q, kv_c, widx, wmask, comp, cidx, sk, out, lse)
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        query, kv, window_indices, window_mask, compressed_kv, compressed_indices, sinks = ctx.saved_tensors
-        inputs = [t.detach().requires_grad_(t.requires_grad) if t is not None and t.is_floating_point() else t
-                  for t in (query, kv, compressed_kv, sinks)]
-        with torch.enable_grad():
-            out = sparse_attention_reference(inputs[0], inputs[1], window_indices, window_mask, inputs[2],
-                                             compressed_indices, inputs[3])
-            wrt = [t for t in inputs if t is not None and t.requires_grad]
-            grads = torch.autograd.grad(out, wrt, grad_out, allow_unused=True) if wrt else []
-        it = iter(grads)
-        result = [next(it) if t is not None and t.requires_grad else None for t in inputs]
-        return result[0], result[1], None, None, result[2], None, result[3]
+        q, kv, widx, wmask, comp, cidx, sinks, out, lse = ctx.saved_tensors
+        chunk = None
+        if ctx.deterministic:  # per-edge rows, each KV row summed by one owner in edge order
+            batch, _, heads, dim = q.shape
+            slots = widx.shape[-1] + (0 if cidx is None else cidx.shape[-1])
+            per_token = batch * slots * ((heads + 63) // 64) * dim * 4
+            chunk = max(1, _EDGE_BUFFER_BYTES // per_token)
+        dq, dkv, dcomp, dsink = ext().sparse_attention_bwd(q, kv, widx, wmask, comp, cidx, sinks, out, lse,
+                                                           grad_out.contiguous(), chunk)
+        return (dq.transpose(1, 2), dkv.to(kv.dtype), None, None,
+                dcomp.to(comp.dtype) if ctx.has_comp else None, None,
+                dsink.sum(dim=(0, 1)).to(ctx.sinks_dtype), None)
+
+
+_EDGE_BUFFER_BYTES = 512 * 2 ** 20  # per-chunk edge rows of the deterministic KV gradient
 
 
 def sparse_attention(query, kv, window_indices, window_mask, compressed_kv, compressed_indices, sinks, *,
                      dropout: float = 0.0, deterministic: bool = False):
     if on_gpu(query) and _sparse_kernel_ok(query, kv, window_indices, compressed_kv, compressed_indices, dropout):
         return _SparseAttention.apply(query, kv, window_indices, window_mask, compressed_kv, compressed_indices,
-                                      sinks)
+                                      sinks, deterministic)
     return sparse_attention_reference(query, kv, window_indices, window_mask, compressed_kv, compressed_indices,
                                       sinks, dropout=dropout)
 

@@ -7,7 +7,11 @@ semantics), writes the new master and the rounded bf16 parameter. With ``in_back
 update of a parameter runs from its post-accumulate-grad hook, so gradients never accumulate for
 the whole model (no global-norm clipping in that mode). ``side_stream=True`` runs those updates on
 a stream of their own, so the memory-bound update of one parameter overlaps the backward GEMMs of
-the next; ``finish_step()`` then orders the caller's stream after them.
+the next; ``finish_step()`` then orders the caller's stream after them. A gradient handed to the
+side stream stays referenced until the caller's stream has waited for its update (at most
+``_IN_FLIGHT`` updates behind), so its memory is never reused early and no ``record_stream`` is
+needed, which keeps the step capturable in a CUDA graph. On the GPU the step count also lives in
+device memory (advanced by ``begin_step``), so a captured step replays with fresh bias corrections.
 
 On CPU the same math runs in plain PyTorch.
 """
@@ -15,11 +19,15 @@ On CPU the same math runs in plain PyTorch.
 from __future__ import annotations
 
 import math
+from collections import deque
 
 import torch
 
 from ..ops import ext
 from ..runtime import local_tensor
+
+
+_IN_FLIGHT = 4  # side-stream updates the caller's stream may run ahead of
 
 
 class FusedAdamW:
@@ -42,6 +50,8 @@ class FusedAdamW:
         self.in_backward = in_backward
         device = self.params[0].device if self.params else torch.device("cpu")
         self.stream = torch.cuda.Stream(device=device) if side_stream and device.type == "cuda" else None
+        self._inflight: deque = deque()
+        self._step_t = torch.zeros(1, dtype=torch.int32, device=device) if device.type == "cuda" else None
         self._hooks = []
         self._pending_step = False
         if in_backward:
@@ -56,16 +66,19 @@ class FusedAdamW:
     def begin_step(self) -> None:
         """In-backward mode: advance the step counter before the backward that applies it."""
         self.step_count += 1
+        if self._step_t is not None:
+            self._step_t.add_(1)
 
     def finish_step(self) -> None:
         """Order the current stream after the updates queued on the side stream (no-op without one)."""
         if self.stream is not None:
             torch.cuda.current_stream(self.stream.device).wait_stream(self.stream)
+            self._inflight.clear()
 
     def step(self, clip_coefficient: torch.Tensor | None = None) -> None:
         if self.in_backward:
             return
-        self.step_count += 1
+        self.begin_step()
         for p in self.params:
             if p.grad is not None:
                 self._update(p, clip_coefficient)
@@ -77,6 +90,8 @@ class FusedAdamW:
 
     def load_state_dict(self, state: dict) -> None:
         self.step_count = int(state["step"])
+        if self._step_t is not None:
+            self._step_t.fill_(self.step_count)
         for p, saved in zip(self.params, state["state"]):
             for key in ("master", "m", "v"):
                 self.state[id(p)][key].copy_(saved[key])
@@ -89,13 +104,20 @@ class FusedAdamW:
     # -- internals -----------------------------------------------------------------------------
     def _hook(self, p: torch.Tensor) -> None:
         if self.step_count == 0:
-            self.step_count = 1
+            self.begin_step()
         if self.stream is not None:
-            self.stream.wait_stream(torch.cuda.current_stream(self.stream.device))
+            main = torch.cuda.current_stream(self.stream.device)
+            self.stream.wait_stream(main)
             grad = local_tensor(p.grad)
             with torch.cuda.stream(self.stream):
                 self._update(p, None)
-            grad.record_stream(self.stream)  # the gradient's memory outlives its use on the side stream
+                done = torch.cuda.Event()
+                done.record(self.stream)
+            self._inflight.append((grad, done))
+            while len(self._inflight) > _IN_FLIGHT:  # the oldest gradient may be released once the
+                old, event = self._inflight.popleft()  # caller's stream is ordered after its update
+                main.wait_event(event)
+                del old
         else:
             self._update(p, None)
         p.grad = None
@@ -109,7 +131,8 @@ class FusedAdamW:
         if data.is_cuda:
             out = data if data.dtype == torch.bfloat16 else None
             ext().adamw_step(st["master"], grad.contiguous(), st["m"], st["v"], out, self.lr, beta1, beta2,
-                             self.eps, self.weight_decay, self.step_count, self.grad_scale, clip_coefficient)
+                             self.eps, self.weight_decay, self.step_count, self.grad_scale, clip_coefficient,
+                             self._step_t if self._step_t is not None and self._step_t.device == data.device else None)
             if out is None:
                 data.copy_(st["master"])
             return

@@ -68,6 +68,9 @@ class TokenDispatcher:
         self.size = 1
         self.rank = 0
 
+    def end_step(self) -> None:
+        """Called once per training step after its backward; the local dispatcher keeps no state."""
+
     def expert_range(self, num_experts: int) -> tuple[int, int]:
         if num_experts < 1:
             raise ValueError("num_experts must be positive")

@@ -72,12 +72,35 @@ class _Workspace:
         self.peer_retw = table("retw")
         self.peer_flags = [table("flags", row * ep * 4) for row in range(5)]
         self.done = torch.zeros(2, dtype=torch.int32, device=device)
+        # Epoch of an exchange = device base + host offset. The offsets count this step's exchanges
+        # and the bases advance on the stream at end_step(), so a CUDA graph captured over a step
+        # replays with fresh epochs. Without end_step() calls the bases stay 0 and the offsets
+        # are plain running epochs.
+        self.epoch_base = torch.zeros(2, dtype=torch.int32, device=device)  # [recv, ret]
         self.recv_epoch = 0
         self.ret_epoch = 0
+        self.any_recv = False  # a slab was filled before: wait for its release before the next push
+        self.any_ret = False
         self._handles = handles
 
     def flag_row(self, row: int) -> torch.Tensor:
         return self.flags[row]
+
+    def recv_base(self) -> torch.Tensor:
+        return self.epoch_base[0:1]
+
+    def ret_base(self) -> torch.Tensor:
+        return self.epoch_base[1:2]
+
+    def end_step(self) -> None:
+        """Fold this step's exchanges into the device bases (one small kernel, stream-ordered)."""
+        # scalar adds: the amounts are kernel arguments, so a captured graph replays them as they are
+        if self.recv_epoch:
+            self.epoch_base[0:1].add_(self.recv_epoch)
+        if self.ret_epoch:
+            self.epoch_base[1:2].add_(self.ret_epoch)
+        self.recv_epoch = 0
+        self.ret_epoch = 0
 
     def check_canaries(self, where: str) -> None:
         """Debug mode only (synchronises): raise if a guard row after a slab was overwritten."""
@@ -112,36 +135,38 @@ class _Exchange:
     def push_to_receivers(self, rows: torch.Tensor, ids=None, weights=None) -> None:
         """rows [T, H] -> every destination's recv slab (waits until the slab is free)."""
         ws, C = self.ws, ops.ext()
-        if ws.recv_epoch > 0:
-            C.ep_wait(ws.flag_row(_RECV_FREE), ws.recv_epoch)
+        if ws.any_recv:  # the previous contents of the peers' slabs were released
+            C.ep_wait(ws.flag_row(_RECV_FREE), ws.recv_epoch, ws.recv_base())
+        ws.any_recv = True
         ws.recv_epoch += 1
         with_meta = ids is not None
         C.ep_push_rows(rows.contiguous(), self.dest_mask, self.slot, ws.peer_recv,
                        ws.peer_meta if with_meta else None, ids, weights, ws.t_cap, self.e_local, ws.done[0:1],
                        ws.peer_flags[_RECV_READY], ws.peer_flags[_COUNTS] if with_meta else None,
-                       self.counts if with_meta else None, ws.rank, ws.recv_epoch)
-        C.ep_wait(ws.flag_row(_RECV_READY), ws.recv_epoch)
+                       self.counts if with_meta else None, ws.rank, ws.recv_epoch, ws.recv_base())
+        C.ep_wait(ws.flag_row(_RECV_READY), ws.recv_epoch, ws.recv_base())
         ws.check_canaries("dispatch")
 
     def release_recv(self) -> None:
         ws = self.ws
-        ops.ext().ep_signal(ws.peer_flags[_RECV_FREE], None, None, ws.rank, ws.recv_epoch)
+        ops.ext().ep_signal(ws.peer_flags[_RECV_FREE], None, None, ws.rank, ws.recv_epoch, ws.recv_base())
 
     def push_to_sources(self, y: torch.Tensor, route: torch.Tensor, weights=None, extra=None) -> None:
         """Per received row: sum_j w_j * y[route[row, j]] -> the source's ret slab (+ extra floats)."""
         ws, C = self.ws, ops.ext()
-        if ws.ret_epoch > 0:
-            C.ep_wait(ws.flag_row(_RET_FREE), ws.ret_epoch)
+        if ws.any_ret:
+            C.ep_wait(ws.flag_row(_RET_FREE), ws.ret_epoch, ws.ret_base())
+        ws.any_ret = True
         ws.ret_epoch += 1
         C.ep_combine_push(y.contiguous(), route, weights, self.recv_counts, ws.peer_ret, extra,
                           ws.peer_retw if extra is not None else None, ws.t_cap, ws.done[1:2],
-                          ws.peer_flags[_RET_READY], ws.rank, ws.ret_epoch)
-        C.ep_wait(ws.flag_row(_RET_READY), ws.ret_epoch)
+                          ws.peer_flags[_RET_READY], ws.rank, ws.ret_epoch, ws.ret_base())
+        C.ep_wait(ws.flag_row(_RET_READY), ws.ret_epoch, ws.ret_base())
         ws.check_canaries("combine")
 
     def release_ret(self) -> None:
         ws = self.ws
-        ops.ext().ep_signal(ws.peer_flags[_RET_FREE], None, None, ws.rank, ws.ret_epoch)
+        ops.ext().ep_signal(ws.peer_flags[_RET_FREE], None, None, ws.rank, ws.ret_epoch, ws.ret_base())
 
 
 class _Dispatch(torch.autograd.Function):
@@ -277,6 +302,11 @@ class NVLinkTokenDispatcher(TokenDispatcher):
         self.num_experts = num_experts
         local = num_experts // self.size
         return self.rank * local, (self.rank + 1) * local
+
+    def end_step(self) -> None:
+        """Advance the device-side exchange epochs past this step (see ``_Workspace.end_step``)."""
+        if self._ws is not None:
+            self._ws.end_step()
 
     def _workspace(self, tokens: int, hidden: int, k: int, device) -> _Workspace:
         ws = self._ws

@@ -22,6 +22,8 @@ keeps them replicated in bf16 and shards only what is large: the fp32 master and
 
 Unit kernels are enqueued in one fixed order on every rank (the order of ``units`` reversed, the
 order in which backward produces them); a unit that completes early waits for its predecessors.
+The step count and the flag epoch live in device memory (advanced by ``begin_step``), so a CUDA
+graph captured over a training step replays with fresh epochs and bias corrections.
 
 Without CUDA (gloo ranks on CPU, the test-suite) the same bookkeeping runs with an all-reduce
 and an all-gather in place of the kernel.
@@ -135,6 +137,10 @@ class PeerShardedOptimizer:
         self.order = list(reversed(self.units))  # the order backward completes them
         self._next = 0
         self.nonfinite = torch.zeros(1, dtype=torch.int32, device=device)
+        # device copies of the step count (bias corrections; restored with the state) and of the flag
+        # epoch (only ever grows: the flags of earlier steps still hold their epochs)
+        self._step_t = torch.zeros(1, dtype=torch.int32, device=device) if self.cuda else None
+        self._epoch_t = torch.zeros(1, dtype=torch.int32, device=device) if self.cuda else None
         self.stream = torch.cuda.Stream(device=device) if self.cuda else None
         self._hooks = [p.register_post_accumulate_grad_hook(self._hook) for u in self.units for p in u.params]
 
@@ -175,6 +181,9 @@ class PeerShardedOptimizer:
     def begin_step(self) -> None:
         self.step_count += 1
         self.epoch += 1
+        if self._step_t is not None:
+            self._step_t.add_(1)
+            self._epoch_t.add_(1)
         self._next = 0
         for unit in self.units:
             unit.pending = len(unit.params)
@@ -199,8 +208,8 @@ class PeerShardedOptimizer:
         C = ext()
         with torch.cuda.stream(self.stream):
             if self.world > 1:
-                C.ep_signal(self.peer_barrier, None, None, self.rank, self.epoch)
-                C.ep_wait(self.flags[self.flag_rows - 1], self.epoch)
+                C.ep_signal(self.peer_barrier, None, None, self.rank, 0, self._epoch_t)
+                C.ep_wait(self.flags[self.flag_rows - 1], 0, self._epoch_t)
         torch.cuda.current_stream(self.device).wait_stream(self.stream)
 
     def remove_hooks(self) -> None:
@@ -247,10 +256,10 @@ class PeerShardedOptimizer:
             self.stream.wait_stream(main)
             with torch.cuda.stream(self.stream):
                 ext().peer_update(self.peer_grad, self.peer_param, self.peer_flags, self.flags, unit.index,
-                                  self.rank, self.epoch, lo, st["master"], st.get("m"), st.get("v"),
+                                  self.rank, 0, lo, st["master"], st.get("m"), st.get("v"),
                                   0 if self.algo == "adamw" else 1, self.lr, self.betas[0], self.betas[1], self.eps,
                                   self.weight_decay, self.step_count, self.grad_scale, None, self.nonfinite,
-                                  self.max_blocks)
+                                  self.max_blocks, self._step_t, self._epoch_t)
             return
         span = slice(unit.start, unit.start + unit.shard * self.world)
         grad = self.grad_pool[span].float()
@@ -285,6 +294,8 @@ class PeerShardedOptimizer:
         if int(state["world"]) != self.world:
             raise ValueError("optimizer state was saved with a different world size")
         self.step_count = int(state["step"])
+        if self._step_t is not None:  # the flag epoch keeps counting from this process's history
+            self._step_t.fill_(self.step_count)
         with torch.no_grad():
             for st, saved in zip(self.state, state["state"]):
                 for key, value in saved.items():

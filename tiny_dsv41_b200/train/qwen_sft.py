@@ -51,7 +51,8 @@ def _init_on_device(model: Qwen3MoeForCausalLM, seed: int, rank: int) -> None:
 class QwenTrainer:
     def __init__(self, config: Qwen3MoeConfig, *, lr: float = 1e-5, moment_dtype=torch.float32,
                  dispatcher: str = "auto", gradient_checkpointing: bool = True, seed: int = 0,
-                 tokens_per_rank: int = 4096, cp_size: int = 1, dense_sync: str = "auto") -> None:
+                 tokens_per_rank: int = 4096, cp_size: int = 1, dense_sync: str = "auto",
+                 cuda_graph: bool = False, graph_warmup: int = 2) -> None:
         self.runtime = initialize_runtime(require_distributed=int(os.environ.get("WORLD_SIZE", "1")) > 1,
                                           timeout_seconds=900)
         rt = self.runtime
@@ -70,6 +71,7 @@ class QwenTrainer:
             token_dispatcher = self._make_dispatcher(dispatcher)
         else:
             token_dispatcher = TokenDispatcher()
+        self.dispatcher = token_dispatcher
         with torch.device("meta"):
             model = Qwen3MoeForCausalLM(config, cp, token_dispatcher)
         model = model.to_empty(device=rt.device).to(torch.bfloat16)
@@ -104,6 +106,16 @@ class QwenTrainer:
             dense_opt,
             FusedAdamW(self.expert_params, in_backward=True, grad_scale=1.0 / self.world, side_stream=side, **hyper),
         ]
+        # CUDA graph of a whole training step (forward, backward, in-backward optimizer, NVLink
+        # exchanges): captured after `graph_warmup` eager steps, then replayed. Every per-step value a
+        # kernel needs (exchange epochs, step counts) lives in device memory and advances inside the
+        # graph, so a replay is one launch from the host instead of several thousand.
+        self.cuda_graph = bool(cuda_graph) and rt.device.type == "cuda"
+        if self.cuda_graph and (cp_size > 1 or self.dense_sync == "fsdp"):
+            raise ValueError("CUDA-graph steps need cp_size 1 and dense_sync 'peer' (no NCCL inside the step)")
+        self.graph_warmup = graph_warmup
+        self._eager_steps = 0
+        self._graph = None
 
     def _make_dispatcher(self, kind: str):
         if kind in ("auto", "nvlink"):
@@ -146,18 +158,50 @@ class QwenTrainer:
                 module.set_modules_to_backward_prefetch([module])
 
     def train_step(self, input_ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        """One optimizer step; returns the loss as a device scalar (inputs on the host or device)."""
+        if self._graph is not None:
+            self._static_ids.copy_(input_ids, non_blocking=True)
+            self._static_labels.copy_(labels, non_blocking=True)
+            self._graph.replay()
+            return self._static_loss
+        if self.cuda_graph and self._eager_steps >= self.graph_warmup:
+            return self._capture(input_ids, labels)
         device = self.runtime.device
-        input_ids = input_ids.to(device, non_blocking=True)
-        labels = labels.to(device, non_blocking=True)
+        loss = self._step(input_ids.to(device, non_blocking=True), labels.to(device, non_blocking=True))
+        self._eager_steps += 1
+        return loss
+
+    def _step(self, input_ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
         for opt in self.optimizers:
             opt.begin_step()
         out = self.model(input_ids, labels=labels, output_router_logits=True)
         out.loss.backward()
         for opt in self.optimizers:
             opt.finish_step()
+        self.dispatcher.end_step()
         return out.loss.detach()
 
+    def _capture(self, input_ids: torch.Tensor, labels: torch.Tensor) -> torch.Tensor:
+        """Capture one step into a CUDA graph (nothing runs during capture), then run it once."""
+        import gc
+
+        device = self.runtime.device
+        self._static_ids = torch.empty(input_ids.shape, dtype=input_ids.dtype, device=device)
+        self._static_labels = torch.empty(labels.shape, dtype=labels.dtype, device=device)
+        self._static_ids.copy_(input_ids, non_blocking=True)
+        self._static_labels.copy_(labels, non_blocking=True)
+        torch.cuda.synchronize(device)
+        gc.collect()
+        torch.cuda.empty_cache()  # eager-step blocks go back, the graph's private pool takes their place
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            loss = self._step(self._static_ids, self._static_labels)
+        self._graph, self._static_loss = graph, loss
+        graph.replay()
+        return loss
+
     def close(self) -> None:
+        self._graph = None
         for opt in self.optimizers:
             opt.remove_hooks()
         if dist.is_initialized():
@@ -173,7 +217,8 @@ class QwenSFTBench:
         self.cp = getattr(args, "cp", 1)
         self.trainer = QwenTrainer(config, lr=args.lr, moment_dtype=moment, dispatcher=args.dispatcher,
                                    tokens_per_rank=args.batch_size * args.seq_len // self.cp, cp_size=self.cp,
-                                   dense_sync=getattr(args, "dense_sync", "auto"))
+                                   dense_sync=getattr(args, "dense_sync", "auto"),
+                                   cuda_graph=getattr(args, "cuda_graph", False))
         self.config = config
 
     def _batch(self, gen: torch.Generator):
@@ -275,6 +320,7 @@ class QwenSFTBench:
                                 if rt.world_size > 1 else "single-gpu"),
                 "optimizer": f"AdamW in-backward, fp32 master, {a.moment_dtype} moments",
                 "dense_sync": t.dense_sync,
+                "cuda_graph": t._graph is not None,
                 "grad_ckpt": True, "l2": "256 MB buffer written between timed steps",
                 "loss_tokens": "last 50%",
             },
