@@ -111,8 +111,27 @@ class CSA2Mode(str, Enum):
     REUSE = "reuse"
 
 
+def complete_group_starts(positions: torch.Tensor, live: torch.Tensor, sequence_ids: torch.Tensor, ratio: int):
+    """Token index of the first member of every complete compression group, packed to the left of
+    each row ([B, L // ratio], unused slots 0), and the number of groups per row.
+
+    A group opens at a live token whose position is a multiple of ``ratio`` and is complete when
+    its last member (``ratio - 1`` tokens later) exists, is live and belongs to the same sequence
+    (packed rows hold several sequences)."""
+    batch, length = positions.shape
+    token = torch.arange(length, device=positions.device)
+    last = token + ratio - 1
+    last_row = last.clamp_max(length - 1).expand(batch, -1)
+    opens = live & (positions % ratio == 0) & (last < length)
+    opens = opens & live.gather(1, last_row) & (sequence_ids == sequence_ids.gather(1, last_row))
+    slot = torch.where(opens, opens.long().cumsum(-1) - 1, length)  # closed groups go to a spare column
+    packed = positions.new_zeros(batch, length + 1).scatter_(1, slot, token.expand(batch, -1))
+    return packed[:, :length // ratio], opens.sum(-1)
+
+
 class Compressor(nn.Module):
-    """Pools complete groups of `ratio` live tokens into global KV latents."""
+    """Pools complete groups of `ratio` live tokens into global KV latents (a softmax-gated
+    weighted sum of the group's projections when ratio > 1, the projection itself otherwise)."""
 
     def __init__(self, config: DeepSeekV41Config, layer_id: int) -> None:
         super().__init__()
@@ -122,40 +141,25 @@ class Compressor(nn.Module):
         self.norm = RMSNorm(config.head_dim, config.rms_norm_eps)
 
     def forward(self, x, positions, token_mask, sequence_ids):
-        batch, length, _ = x.shape
-        live = token_mask.bool()
-        ends = torch.arange(length, device=x.device) + self.ratio - 1
-        safe = ends.clamp_max(length - 1).expand(batch, -1)
-        complete = live & positions.remainder(self.ratio).eq(0) & ends.lt(length)
-        complete &= live.gather(1, safe) & sequence_ids.eq(sequence_ids.gather(1, safe))
-        group_counts = complete.long().sum(-1)
-        if self.gate_proj is None:
-            kv = self.kv_proj(x)
-            gate = None
-        else:
-            kv = F.linear(x.float(), self.kv_proj.weight.float())
-            gate = F.linear(x.float(), self.gate_proj.weight.float())
-        dest = torch.where(complete, complete.long().cumsum(-1) - 1, length)
-        order = positions.new_zeros(batch, length + 1)
-        order.scatter_(1, dest, torch.arange(length, device=x.device).expand(batch, -1))
-        max_groups = length // self.ratio
-        starts = order[:, :max_groups]
-        index = (starts.unsqueeze(-1) + torch.arange(self.ratio, device=x.device)).flatten(1)
-        group_positions = positions.gather(1, starts)
-        group_sequence_ids = sequence_ids.gather(1, starts)
-        valid = torch.arange(max_groups, device=x.device) < group_counts.unsqueeze(-1)
-        group_positions = group_positions.masked_fill(~valid, 0)
-        group_sequence_ids = group_sequence_ids.masked_fill(~valid, -1)
-        if max_groups == 0:
+        starts, count = complete_group_starts(positions, token_mask.bool(), sequence_ids, self.ratio)
+        groups = starts.shape[1]
+        valid = torch.arange(groups, device=x.device) < count.unsqueeze(-1)
+        group_positions = positions.gather(1, starts).masked_fill(~valid, 0)
+        group_sequence_ids = sequence_ids.gather(1, starts).masked_fill(~valid, -1)
+        if groups == 0:
             return None, group_positions, group_sequence_ids, valid
-        gathered = kv.gather(1, index.unsqueeze(-1).expand(-1, -1, kv.shape[-1]))
-        if gate is None:
-            latent = gathered
-        else:
-            g = gate.gather(1, index.unsqueeze(-1).expand(-1, -1, gate.shape[-1]))
-            gathered = gathered.view(batch, max_groups, self.ratio, -1).float()
-            g = g.view(batch, max_groups, self.ratio, -1)
-            latent = (gathered * g.softmax(dim=2)).sum(dim=2)
+        members = (starts.unsqueeze(-1) + torch.arange(self.ratio, device=x.device)).flatten(1)
+
+        def take(values):  # [B, groups * ratio, D] rows of the group members
+            return values.gather(1, members.unsqueeze(-1).expand(-1, -1, values.shape[-1]))
+
+        if self.gate_proj is None:
+            latent = take(self.kv_proj(x))
+        else:  # pooled in fp32
+            batch = x.shape[0]
+            kv = take(F.linear(x.float(), self.kv_proj.weight.float())).view(batch, groups, self.ratio, -1)
+            gate = take(F.linear(x.float(), self.gate_proj.weight.float())).view(batch, groups, self.ratio, -1)
+            latent = (kv * gate.softmax(dim=2)).sum(dim=2)
         latent = latent.masked_fill(~valid.unsqueeze(-1), 0)
         return self.norm(latent.to(x.dtype)), group_positions, group_sequence_ids, valid
 
@@ -200,66 +204,76 @@ def select_candidate_blocks(scores, visible, topk_blocks, block_size, *, stable=
     return keep.repeat_interleave(block_size, dim=-1)[..., :width]
 
 
+def visible_key_ranges(key_sequence_ids: torch.Tensor, query_sequence_ids: torch.Tensor, positions: torch.Tensor,
+                       ratio: int):
+    """Per query, the compressed keys it may see: ``[start, end)`` in the key axis (keys are sorted
+    by sequence; a query sees its own sequence's keys whose groups ended at or before it), the
+    width of the widest sequence (a host integer: it shapes the score tensor) and validity."""
+    sentinel = torch.iinfo(key_sequence_ids.dtype).max
+    searchable = key_sequence_ids.masked_fill(key_sequence_ids < 0, sentinel).contiguous()
+    queries = query_sequence_ids.contiguous()
+    first = torch.searchsorted(searchable, queries, right=False)
+    past = torch.searchsorted(searchable, queries, right=True)
+    end = torch.minimum(past, first + (positions + 1) // ratio)
+    valid = (query_sequence_ids >= 0) & (first < end)
+    return first, torch.where(valid, end, first), int((past - first).max().item())
+
+
 class SparseIndexer(nn.Module):
+    """Scores the compressed keys for every query (relu(q . k) weighted per head) and keeps the
+    top-k. A layer that owns keys projects them from this layer's latents; the candidate-source
+    layer also keeps the best key blocks, which later layers restrict their scores to."""
+
     def __init__(self, config: DeepSeekV41Config, layer_id: int, rotary: RotaryEmbedding) -> None:
         super().__init__()
-        self.stable_topk = False
+        source = config.candidate_source_layer_id
         self.owns_keys = layer_id in config.kv_source_layer_ids
-        self.is_candidate_source = layer_id == config.candidate_source_layer_id
-        self.uses_candidates = 0 <= config.candidate_source_layer_id < layer_id
-        self.num_heads = config.index_n_heads
-        self.head_dim = config.index_head_dim
-        self.topk = config.index_topk
-        self.topk_blocks = config.candidate_topk_blocks
-        self.block_size = config.candidate_block_size
-        self.quantized_cache = config.cache_quantization == "hf"
+        self.is_candidate_source = layer_id == source
+        self.uses_candidates = 0 <= source < layer_id
         self.ratio = config.compress_ratios[layer_id]
         self.rotary = rotary
+        self.stable_topk = False  # set by callers that need ties broken by index (parity runs)
+        self.quantized_cache = config.cache_quantization == "hf"
+        self.num_heads, self.head_dim, self.topk = config.index_n_heads, config.index_head_dim, config.index_topk
+        self.topk_blocks, self.block_size = config.candidate_topk_blocks, config.candidate_block_size
+        # parameter names are the checkpoint's
         self.q_proj = Linear(config.q_lora_rank, self.num_heads * self.head_dim, bias=False)
         self.weight_proj = Linear(config.hidden_size, self.num_heads, bias=False)
         if self.owns_keys:
             self.k_proj = Linear(config.head_dim, self.head_dim, bias=False)
             self.k_norm = RMSNorm(self.head_dim, config.rms_norm_eps)
 
+    def _fp4(self, t: torch.Tensor) -> torch.Tensor:
+        return quantize_activation(t, "fp4_index") if self.quantized_cache else t
+
+    def _refresh_keys(self, latent, group_positions, shadow: ShadowIndexers) -> None:
+        shadow.index_keys = None
+        if latent is not None:
+            keys = apply_rope(self.k_norm(self.k_proj(latent)), group_positions, self.rotary.freqs(True))
+            shadow.index_keys = self._fp4(keys).unsqueeze(1)
+
     def forward(self, x, q_residual, latent, group_positions, context: ModelContext, shadow: ShadowIndexers):
-        batch, length, _ = x.shape
         if self.owns_keys:
-            shadow.index_keys = None
-            if latent is not None:
-                keys = apply_rope(self.k_norm(self.k_proj(latent)), group_positions, self.rotary.freqs(True))
-                if self.quantized_cache:
-                    keys = quantize_activation(keys, "fp4_index")
-                shadow.index_keys = keys.unsqueeze(1)
-        if shadow.index_keys is None:
+            self._refresh_keys(latent, group_positions, shadow)
+        if shadow.index_keys is None:  # nothing compressed yet: no selection (and no candidates)
             shadow.topk_indices = None
             if self.is_candidate_source:
                 shadow.candidates = None
             return
-        keys = shadow.index_keys[:, 0]
-        key_seq = shadow.compressed_sequence_ids
-        sentinel = torch.iinfo(key_seq.dtype).max
-        searchable = key_seq.masked_fill(key_seq < 0, sentinel).contiguous()
-        query_ids = context.sequence_ids.contiguous()
-        starts = torch.searchsorted(searchable, query_ids, right=False)
-        seq_ends = torch.searchsorted(searchable, query_ids, right=True)
-        visible = (context.positions + 1) // self.ratio
-        ends = torch.minimum(seq_ends, starts + visible)
-        valid = (context.sequence_ids >= 0) & (starts < ends)
-        ends = torch.where(valid, ends, starts)
+        batch, length, _ = x.shape
+        first, end, width = visible_key_ranges(shadow.compressed_sequence_ids, context.sequence_ids,
+                                               context.positions, self.ratio)
         query = self.q_proj(q_residual).view(batch, length, self.num_heads, self.head_dim)
-        query = apply_rope(query, context.positions, self.rotary.freqs(True))
-        if self.quantized_cache:
-            query = quantize_activation(query, "fp4_index")
+        query = self._fp4(apply_rope(query, context.positions, self.rotary.freqs(True)))
         head_weights = self.weight_proj(x).float() * self.num_heads ** -0.5
-        width = int((seq_ends - starts).max().item())
-        previous = shadow.candidates if self.uses_candidates else None
-        scores = index_scores(query, keys, head_weights, starts, ends, width, previous)
+        scores = index_scores(query, shadow.index_keys[:, 0], head_weights, first, end, width,
+                              shadow.candidates if self.uses_candidates else None)
         if self.is_candidate_source:
-            shadow.candidates = select_candidate_blocks(scores, ends - starts, self.topk_blocks, self.block_size,
+            shadow.candidates = select_candidate_blocks(scores, end - first, self.topk_blocks, self.block_size,
                                                         stable=self.stable_topk)
         values, idx = _select_topk(scores, min(self.topk, scores.shape[-1]), stable=self.stable_topk,
                                    sorted=self.quantized_cache)
-        picked = starts.unsqueeze(-1) + idx
+        picked = first.unsqueeze(-1) + idx
         shadow.topk_indices = torch.where(values > float("-inf"), picked, torch.full_like(picked, -1))
 
 
@@ -329,4 +343,5 @@ class CSA2Attention(nn.Module):
 
 
 __all__ = ["AttentionSinks", "CSA2Attention", "CSA2Mode", "Compressor", "GroupedLinear", "RMSNorm",
-           "RotaryEmbedding", "ShadowIndexers", "SparseIndexer", "apply_rope", "select_candidate_blocks"]
+           "RotaryEmbedding", "ShadowIndexers", "SparseIndexer", "apply_rope", "complete_group_starts",
+           "select_candidate_blocks", "visible_key_ranges"]
