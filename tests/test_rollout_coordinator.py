@@ -78,3 +78,63 @@ def test_cli_run(tmp_path, capsys):
     summary = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert summary["episodes"] == 4 and summary["eligible"] == 4
     assert (tmp_path / "out" / "summary.json").is_file()
+
+
+class _Lifecycle(_Echo):
+    def __init__(self, **kw):
+        super().__init__(**kw)
+        self.starts = self.closes = 0
+
+    async def start(self):
+        self.starts += 1
+
+    async def close(self):
+        self.closes += 1
+
+
+def test_persistent_stream_session():
+    backend = _Lifecycle()
+
+    async def scenario():
+        coord = Coordinator({"prompt-response": backend}, max_workers=2, max_groups=1)
+        await coord.open_stream(max_pending=3)
+        plans = _plans(groups=3, size=3)
+        first = await coord.execute_stream_group(plans[0:3], sequence=0)
+        assert [r.identity.sample_index for r in first] == [0, 1, 2]
+        with pytest.raises(ValueError):  # a replayed sequence number
+            await coord.execute_stream_group(plans[3:6], sequence=0)
+        with pytest.raises(ValueError):  # two groups at once
+            await coord.execute_stream_group(plans[2:5], sequence=5)
+        with pytest.raises(ValueError):  # more pending episodes than the credit
+            await coord.execute_stream_group(plans[3:6] + [plans[6]], sequence=6)
+        await coord.execute_stream_group(plans[3:6], sequence=7)
+        await coord.pause_stream()
+        with pytest.raises(ValueError):  # paused: no admission
+            await coord.execute_stream_group(plans[6:9], sequence=8)
+        coord.resume_stream()
+        await coord.execute_stream_group(plans[6:9], sequence=9)
+        await coord.close_stream()
+        return coord
+
+    coord = asyncio.run(scenario())
+    assert backend.starts == 1 and backend.closes == 1
+    assert backend.peak <= 2 and coord.quarantined == 0
+
+
+def test_stream_stops_after_uncertain_request():
+    backend = _Lifecycle(uncertain_for={1})
+
+    async def scenario():
+        coord = Coordinator({"prompt-response": backend}, max_workers=3)
+        await coord.open_stream(max_pending=3)
+        plans = _plans(groups=2, size=3)
+        await coord.execute_stream_group(plans[:3], sequence=1)
+        with pytest.raises(ValueError):
+            await coord.execute_stream_group(plans[3:], sequence=2)
+        with pytest.raises(RuntimeError):
+            coord.resume_stream()
+        await coord.close_stream()
+        return coord
+
+    coord = asyncio.run(scenario())
+    assert coord.quarantined == 1
