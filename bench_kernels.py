@@ -128,7 +128,37 @@ def cases():
         flops = 2 * batch * seq * width * heads * dim
         return (lambda: C.index_scores(q, k, w, starts, ends, width, None)), None, flops, None
 
+    def sparse_attention(kind, batch=1, seq=4096, heads=64, dim=512, window=128, selected=512, comp_ratio=4):
+        # DeepSeek-V4-Flash-like sparse attention: 64 heads share one 512-wide latent KV row per key;
+        # each token sees its 128 window keys and 512 selected compressed keys (plus the sink).
+        # FLOPs: QK^T and PV per (token, head, key); the reference is the gathered PyTorch
+        # restatement (einsum on gathered [B, L, keys, D] tensors) timed on the same inputs.
+        from tiny_dsv41_b200.ops.sparse_attention import sparse_attention_reference
+
+        comp_len = seq // comp_ratio
+        q = torch.randn(batch, seq, heads, dim, device=dev, dtype=bf)
+        kv = torch.randn(batch, seq, dim, device=dev, dtype=bf)
+        comp = torch.randn(batch, comp_len, dim, device=dev, dtype=bf)
+        pos = torch.arange(seq, device=dev).view(1, -1, 1)
+        widx = (pos - window + 1 + torch.arange(window, device=dev).view(1, 1, -1))
+        wmask = (widx >= 0).expand(batch, -1, -1).contiguous()
+        widx = widx.clamp_min(0).expand(batch, -1, -1).contiguous()
+        sel = torch.randint(0, comp_len, (batch, seq, selected), device=dev)
+        sinks = torch.randn(heads, device=dev)
+        keys = window + selected
+        fwd_flops = 4 * batch * seq * heads * keys * dim
+        if kind == "fwd":
+            return ((lambda: C.sparse_attention_fwd(q, kv, widx, wmask, comp, sel, sinks)),
+                    (lambda: sparse_attention_reference(q.transpose(1, 2), kv, widx, wmask, comp, sel, sinks)),
+                    fwd_flops, None)
+        out, lse = C.sparse_attention_fwd(q, kv, widx, wmask, comp, sel, sinks)
+        dout = torch.randn_like(out)
+        return ((lambda: C.sparse_attention_bwd(q, kv, widx, wmask, comp, sel, sinks, out, lse, dout)), None,
+                int(2.5 * fwd_flops), None)
+
     return {
+        "sparse_attn_fwd": lambda: sparse_attention("fwd"),
+        "sparse_attn_bwd": lambda: sparse_attention("bwd"),
         "dense_lm_head": lambda: dense(4096, 151936, 2048),
         "dense_qkv": lambda: dense(4096, 5120, 2048),
         "dense_8192": lambda: dense(8192, 8192, 8192),
@@ -170,7 +200,8 @@ def main(argv=None) -> None:
             row.update(gbs=round(nbytes / ms / 1e6, 1), frac_of_peak=round(nbytes / ms / 1e6 / peaks["gbs"], 3))
         if ref is not None:
             rms = _time(ref, args.iters)
-            label = "cudnn_sdpa" if name.startswith("attn") else "cublas"
+            label = ("cudnn_sdpa" if name.startswith("attn") else "gathered_torch" if name.startswith("sparse")
+                     else "cublas")
             row.update({f"{label}_ms": round(rms, 4), f"{label}_tflops": round(flops / rms / 1e9, 1)})
         row["peak_source"] = peaks["source"]
         print(json.dumps(row), flush=True)
