@@ -27,16 +27,14 @@ def _run(cuda_graph: bool, batches):
 
 def test_cuda_graph_step_matches_eager():
     gen = torch.Generator().manual_seed(0)
-    batches = []
-    for _ in range(6):
-        ids = torch.randint(0, 512, (1, 256), generator=gen)
-        labels = ids.clone()
-        labels[:, :128] = -100
-        batches.append((ids.pin_memory(), labels.pin_memory()))
+    ids = torch.randint(0, 512, (1, 256), generator=gen)
+    labels = ids.clone()
+    labels[:, :128] = -100
+    batches = [(ids.pin_memory(), labels.pin_memory())] * 6  # one batch: the loss must fall
     eager, p_eager, cap0 = _run(False, batches)
     graph, p_graph, cap1 = _run(True, batches)
     assert not cap0 and cap1
-    assert eager[-1] < eager[0]
+    assert eager[-1] < eager[0], eager
     for a, b in zip(eager, graph):
         assert abs(a - b) <= 2e-3 * abs(a), (eager, graph)
     for name, p in p_eager.items():

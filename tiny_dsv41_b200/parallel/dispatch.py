@@ -71,6 +71,9 @@ class TokenDispatcher:
     def end_step(self) -> None:
         """Called once per training step after its backward; the local dispatcher keeps no state."""
 
+    def abort_step(self) -> None:
+        """Forget the exchanges counted for a step that did not run (a failed graph capture)."""
+
     def expert_range(self, num_experts: int) -> tuple[int, int]:
         if num_experts < 1:
             raise ValueError("num_experts must be positive")

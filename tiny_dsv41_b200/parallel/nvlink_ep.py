@@ -308,6 +308,11 @@ class NVLinkTokenDispatcher(TokenDispatcher):
         if self._ws is not None:
             self._ws.end_step()
 
+    def abort_step(self) -> None:
+        """Drop the offsets counted by a step that never ran (a failed CUDA-graph capture)."""
+        if self._ws is not None:
+            self._ws.recv_epoch = self._ws.ret_epoch = 0
+
     def _workspace(self, tokens: int, hidden: int, k: int, device) -> _Workspace:
         ws = self._ws
         if ws is None or ws.t_cap < tokens or ws.hidden != hidden or ws.k != k:

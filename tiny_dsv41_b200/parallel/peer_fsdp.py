@@ -245,6 +245,13 @@ class PeerShardedOptimizer:
                 unit.launched = True
                 self._update(unit)
 
+    def _blocks(self, unit: _Unit) -> int:
+        """CTAs of a unit's update: few while backward GEMMs still run beside it, the whole GPU for
+        the last unit of the step (the embedding), which nothing overlaps."""
+        if unit is self.order[-1]:
+            return max(self.max_blocks, 4 * torch.cuda.get_device_properties(self.device).multi_processor_count)
+        return self.max_blocks
+
     @torch.no_grad()
     def _update(self, unit: _Unit) -> None:
         st = self.state[unit.index]
@@ -259,7 +266,7 @@ class PeerShardedOptimizer:
                                   self.rank, 0, lo, st["master"], st.get("m"), st.get("v"),
                                   0 if self.algo == "adamw" else 1, self.lr, self.betas[0], self.betas[1], self.eps,
                                   self.weight_decay, self.step_count, self.grad_scale, None, self.nonfinite,
-                                  self.max_blocks, self._step_t, self._epoch_t)
+                                  self._blocks(unit), self._step_t, self._epoch_t)
             return
         span = slice(unit.start, unit.start + unit.shard * self.world)
         grad = self.grad_pool[span].float()

@@ -194,8 +194,26 @@ class QwenTrainer:
         gc.collect()
         torch.cuda.empty_cache()  # eager-step blocks go back, the graph's private pool takes their place
         graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
+        try:
+            with torch.cuda.graph(graph):
+                loss = self._step(self._static_ids, self._static_labels)
+        except RuntimeError as error:
+            # Nothing ran during the failed capture, and an eager step issues the same kernels in the
+            # same order with the same device-side epochs, so this rank can carry on eagerly even if
+            # its peers replay graphs.
+            import warnings
+
+            warnings.warn(f"CUDA-graph capture failed, continuing with eager steps: {error}")
+            del graph
+            self.cuda_graph = False
+            torch.cuda.synchronize(device)
+            for opt in self.optimizers:  # the capture's Python-side bookkeeping is rolled back
+                if hasattr(opt, "_inflight"):
+                    opt._inflight.clear()
+            self.dispatcher.abort_step()
             loss = self._step(self._static_ids, self._static_labels)
+            self._eager_steps += 1
+            return loss
         self._graph, self._static_loss = graph, loss
         graph.replay()
         return loss
