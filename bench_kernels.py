@@ -156,7 +156,27 @@ def cases():
         return ((lambda: C.sparse_attention_bwd(q, kv, widx, wmask, comp, sel, sinks, out, lse, dout)), None,
                 int(2.5 * fwd_flops), None)
 
+    def peer_update(n=256 * 1024 * 1024, moments=torch.bfloat16, blocks=1184):
+        # the fused dense-sync kernel of parallel/peer_fsdp.py on one GPU (world 1: the peer
+        # tables hold the local pools), one 256M-element unit with bf16 moments. Bytes per element:
+        # gradient 2 + parameter 2 + master 8 + moments 8 (bf16, read and written) = 20.
+        pool = torch.randn(n, device=dev, dtype=bf)
+        grad = torch.randn(n, device=dev, dtype=bf)
+        flags = torch.zeros(2, 1, dtype=torch.int32, device=dev)
+        master = pool.float()
+        m = torch.zeros(n, device=dev, dtype=moments)
+        v = torch.zeros(n, device=dev, dtype=moments)
+        tables = [torch.tensor([t.data_ptr()], dtype=torch.int64) for t in (grad, pool, flags)]
+        epoch = [0]
+
+        def step():
+            epoch[0] += 1
+            C.peer_update(tables[0], tables[1], tables[2], flags, 0, 0, epoch[0], 0, master, m, v, 0, 1e-4, 0.9,
+                          0.95, 1e-8, 0.1, epoch[0], 1.0, None, None, blocks)
+        return step, None, None, n * (2 + 2 + 8 + 2 * 2 * moments.itemsize)
+
     return {
+        "peer_update": peer_update,
         "sparse_attn_fwd": lambda: sparse_attention("fwd"),
         "sparse_attn_bwd": lambda: sparse_attention("bwd"),
         "dense_lm_head": lambda: dense(4096, 151936, 2048),

@@ -67,8 +67,6 @@ struct SaSmem {
   uint64_t s_free[2];
   uint64_t p_full;
   uint64_t pv_done;
-  const __nv_bfloat16* key_src[kKeys];  // gather table of the tile being loaded
-  uint32_t key_ok[kKeys];
   float red[4][kHeadsCta];
   float m_run[kHeadsCta];
   float l_run[kHeadsCta];
@@ -120,22 +118,32 @@ struct SaParams {
   int* status;
 };
 
-// Global source row of entry j of token (b, t): window entries first, then the selected ones.
-template <int D>
-__device__ __forceinline__ const __nv_bfloat16* key_row(const SaParams& p, int b, int t, int j, bool& ok) {
+// The token's entry table, built once per CTA in its prologue (dynamic shared memory after the
+// fixed part): entry j < W is window row win_idx[j] of the raw KV, entry j >= W is compressed row
+// comp_idx[j - W]; -1 marks a masked, negative or out-of-range entry. The gather and the softmax
+// read it instead of the index arrays in global memory.
+__device__ __forceinline__ void build_entries(const SaParams& p, int b, int t, int32_t* ent) {
   const int64_t tok = static_cast<int64_t>(b) * p.L + t;
-  if (j < p.W) {
-    const int64_t idx = p.win_idx[tok * p.W + j];
-    ok = p.win_mask[tok * p.W + j] != 0 && idx >= 0 && idx < p.S;
-    return p.kv + (static_cast<int64_t>(b) * p.S + (ok ? idx : 0)) * D;
+  for (int j = threadIdx.x; j < p.W + p.K; j += blockDim.x) {
+    int32_t e = -1;
+    if (j < p.W) {
+      const int64_t idx = p.win_idx[tok * p.W + j];
+      if (p.win_mask[tok * p.W + j] != 0 && idx >= 0 && idx < p.S) e = static_cast<int32_t>(idx);
+    } else {
+      const int64_t idx = p.comp_idx[tok * p.K + (j - p.W)];
+      if (idx >= 0 && idx < p.C) e = static_cast<int32_t>(idx);
+    }
+    ent[j] = e;
   }
-  if (j < p.W + p.K) {
-    const int64_t idx = p.comp_idx[tok * p.K + (j - p.W)];
-    ok = idx >= 0 && idx < p.C;
-    return p.comp + (static_cast<int64_t>(b) * p.C + (ok ? idx : 0)) * D;
-  }
-  ok = false;
-  return p.kv;
+}
+__device__ __forceinline__ int32_t entry_at(const SaParams& p, const int32_t* ent, int j) {
+  return j < p.W + p.K ? ent[j] : -1;
+}
+// Global row of entry j (a valid in-range row even for e < 0, whose copy is zero-filled).
+template <int D>
+__device__ __forceinline__ const __nv_bfloat16* entry_src(const SaParams& p, int b, int j, int32_t e) {
+  const int64_t row = e < 0 ? 0 : e;
+  return j < p.W ? p.kv + (static_cast<int64_t>(b) * p.S + row) * D : p.comp + (static_cast<int64_t>(b) * p.C + row) * D;
 }
 
 template <int D>
@@ -144,9 +152,11 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_fwd_kernel(const Sa
   constexpr int kBufs = Cfg::kBufs;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SaSmem<D>& sm = *reinterpret_cast<SaSmem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  int32_t* ent = reinterpret_cast<int32_t*>(&sm + 1);
   const int t = blockIdx.x, b = blockIdx.y, hg = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int entries = p.W + p.K;
+  build_entries(p, b, t, ent);
   const int tiles = (entries + kKeys - 1) / kKeys;
   const int64_t tok = static_cast<int64_t>(b) * p.L + t;
 
@@ -209,20 +219,16 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_fwd_kernel(const Sa
         break;
       }
       const uint32_t kbase = smem_u32(sm.k[buf]);
-      {  // one source row per thread, then consecutive threads copy consecutive chunks of a row
-        bool ok;
-        sm.key_src[pt] = key_row<D>(p, b, t, it * kKeys + pt, ok);
-        sm.key_ok[pt] = ok ? 1u : 0u;
-      }
-      producer_sync();
+      // consecutive threads copy consecutive 16-byte chunks of a key row
       for (int c = pt; c < kKeys * (D / 8); c += 128) {
         const int row = c / (D / 8), ch = c % (D / 8);
-        cp_async16(kbase + (ch >> 3) * kKAtom + swz(row, ch & 7), sm.key_src[row] + ch * 8, sm.key_ok[row] != 0);
+        const int j = it * kKeys + row;
+        const int32_t e = entry_at(p, ent, j);
+        cp_async16(kbase + (ch >> 3) * kKAtom + swz(row, ch & 7), entry_src<D>(p, b, j, e) + ch * 8, e >= 0);
       }
       cp_async_commit();
       cp_async_wait_all();
       fence_proxy_async_smem();
-      producer_sync();  // the gather table is read by every producer before the next tile rewrites it
       mbar_arrive(&sm.k_full[buf]);
     }
   } else if (warp == 4) {
@@ -309,8 +315,7 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_fwd_kernel(const Sa
       }
       tc_fence_before();
       mbar_arrive(&sm.s_free[it & 1]);
-      bool valid;
-      (void)key_row<D>(p, b, t, it * kKeys + row, valid);
+      const bool valid = entry_at(p, ent, it * kKeys + row) >= 0;
 #pragma unroll
       for (int j = 0; j < 64; ++j) s[j] = valid ? s[j] * p.scale_log2 : -INFINITY;
       // per-head tile maximum
@@ -477,8 +482,6 @@ struct SbSmem {
   uint64_t k_full[SbCfg<D>::kBufs];
   uint64_t k_empty[SbCfg<D>::kBufs];
   uint64_t s_full, s_free, ds_full, ds_free, dkv_full, dkv_free, dq_full;
-  const __nv_bfloat16* key_src[kKeys];
-  uint32_t key_ok[kKeys];
   float lse2[kHeadsCta];
   float delta[kHeadsCta];
   float dpart[2][kHeadsCta];
@@ -515,7 +518,9 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_bwd_kernel(const Sb
   const SaParams& p = sp.f;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   SbSmem<D>& sm = *reinterpret_cast<SbSmem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  int32_t* ent = reinterpret_cast<int32_t*>(&sm + 1);
   const int t = sp.t0 + blockIdx.x, b = blockIdx.y, hg = blockIdx.z;
+  build_entries(p, b, t, ent);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles = (p.W + p.K + kKeys - 1) / kKeys;
   const int64_t tok = static_cast<int64_t>(b) * p.L + t;
@@ -572,12 +577,6 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_bwd_kernel(const Sb
       mbar_arrive(&sm.qd_full);
     }
     for (int it = 0; it < tiles; ++it) {
-      {
-        bool ok;
-        sm.key_src[pt] = key_row<D>(p, b, t, it * kKeys + pt, ok);
-        sm.key_ok[pt] = ok ? 1u : 0u;
-      }
-      producer_sync();
       for (int j = 0; j < kLoadsPerTile; ++j) {
         const int n = it * kLoadsPerTile + j;
         const int buf = load_buf(n), half = load_half(n), use = load_use(n);
@@ -588,15 +587,16 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_bwd_kernel(const Sb
         constexpr int kHalfChunks = D / 16;  // 16-byte chunks per half row
         for (int c = pt; c < kKeys * kHalfChunks; c += 128) {
           const int row = c / kHalfChunks, ch = c % kHalfChunks;
-          cp_async16(kb + (ch >> 3) * kKAtom + swz(row, ch & 7), sm.key_src[row] + half * (D / 2) + ch * 8,
-                     sm.key_ok[row] != 0);
+          const int entry = it * kKeys + row;
+          const int32_t e = entry_at(p, ent, entry);
+          cp_async16(kb + (ch >> 3) * kKAtom + swz(row, ch & 7), entry_src<D>(p, b, entry, e) + half * (D / 2) + ch * 8,
+                     e >= 0);
         }
         cp_async_commit();
         cp_async_wait_all();
         fence_proxy_async_smem();
         mbar_arrive(&sm.k_full[buf]);
       }
-      producer_sync();
       if (sm.pfail) break;
     }
   } else if (warp == 4) {
@@ -759,8 +759,9 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_bwd_kernel(const Sb
       }
       tc_fence_before();
       mbar_arrive(&sm.s_free);
-      bool valid;
-      const __nv_bfloat16* src = key_row<D>(p, b, t, it * kKeys + row, valid);
+      const int32_t e_row = entry_at(p, ent, it * kKeys + row);
+      const bool valid = e_row >= 0;
+      const __nv_bfloat16* src = entry_src<D>(p, b, it * kKeys + row, e_row);
       // P and scale * dS
       uint32_t pk[32];
 #pragma unroll
@@ -873,13 +874,16 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_bwd_kernel(const Sb
 
 template <int D>
 void launch_bwd(const SbParams& prm, int tokens, int B, int groups) {
-  const size_t smem = sizeof(SbSmem<D>) + 1024;
-  static bool configured = false;
-  if (!configured) {
-    TDSV_CUDA_CHECK(cudaFuncSetAttribute(sparse_attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem)));
-    configured = true;
-  }
+  const size_t smem = sizeof(SbSmem<D>) + 1024 + static_cast<size_t>(prm.f.W + prm.f.K) * sizeof(int32_t);
+  static const int limit = [] {  // configured once at the device's opt-in maximum
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncSetAttribute(sparse_attn_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+    return v;
+  }();
+  TDSV_CHECK(smem <= static_cast<size_t>(limit), "sparse attention: too many keys per token for shared memory (",
+             smem, " > ", limit, " bytes)");
   sparse_attn_bwd_kernel<D><<<dim3(tokens, B, groups), kSaThreads, smem, stream()>>>(prm);
 }
 
@@ -917,13 +921,16 @@ __global__ void ordered_edge_reduce_kernel(const float* __restrict__ edges, cons
 
 template <int D>
 void launch_fwd(const SaParams& prm, int L, int B, int groups) {
-  const size_t smem = sizeof(SaSmem<D>) + 1024;
-  static bool configured = false;
-  if (!configured) {
-    TDSV_CUDA_CHECK(cudaFuncSetAttribute(sparse_attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(smem)));
-    configured = true;
-  }
+  const size_t smem = sizeof(SaSmem<D>) + 1024 + static_cast<size_t>(prm.W + prm.K) * sizeof(int32_t);
+  static const int limit = [] {  // configured once at the device's opt-in maximum
+    int dev = 0, v = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaFuncSetAttribute(sparse_attn_fwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, v);
+    return v;
+  }();
+  TDSV_CHECK(smem <= static_cast<size_t>(limit), "sparse attention: too many keys per token for shared memory (",
+             smem, " > ", limit, " bytes)");
   sparse_attn_fwd_kernel<D><<<dim3(L, B, groups), kSaThreads, smem, stream()>>>(prm);
 }
 
