@@ -83,7 +83,7 @@ at::Tensor token_logprob_bwd(const at::Tensor& logits, const at::Tensor& targets
 void adamw_step(at::Tensor& master, const at::Tensor& grad, at::Tensor& m, at::Tensor& v,
                 const c10::optional<at::Tensor>& out, double lr, double beta1, double beta2, double eps,
                 double weight_decay, int64_t step, double grad_scale, const c10::optional<at::Tensor>& grad_scale_t,
-                const c10::optional<at::Tensor>& step_t);
+                const c10::optional<at::Tensor>& step_t, int64_t max_blocks);
 void sgd_step(at::Tensor& param, const at::Tensor& grad, const c10::optional<at::Tensor>& out, double lr,
               double grad_scale, const c10::optional<at::Tensor>& nonfinite);
 at::Tensor grad_sq_norm(const at::Tensor& g);
@@ -203,7 +203,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("token_logprob_bwd", &tdsv::token_logprob_bwd);
   m.def("adamw_step", &tdsv::adamw_step, py::arg("master"), py::arg("grad"), py::arg("m"), py::arg("v"),
         py::arg("out"), py::arg("lr"), py::arg("beta1"), py::arg("beta2"), py::arg("eps"), py::arg("weight_decay"),
-        py::arg("step"), py::arg("grad_scale"), py::arg("grad_scale_t"), py::arg("step_t") = py::none());
+        py::arg("step"), py::arg("grad_scale"), py::arg("grad_scale_t"), py::arg("step_t") = py::none(),
+        py::arg("max_blocks") = 0);
   m.def("sgd_step", &tdsv::sgd_step);
   m.def("grad_sq_norm", &tdsv::grad_sq_norm);
   m.def("gemm", &tdsv::gemm);

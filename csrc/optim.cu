@@ -142,7 +142,7 @@ int grid_for(int64_t n) {
 void adamw_step(at::Tensor& master, const at::Tensor& grad, at::Tensor& m, at::Tensor& v,
                 const c10::optional<at::Tensor>& out, double lr, double beta1, double beta2, double eps,
                 double weight_decay, int64_t step, double grad_scale, const c10::optional<at::Tensor>& grad_scale_t,
-                const c10::optional<at::Tensor>& step_t) {
+                const c10::optional<at::Tensor>& step_t, int64_t max_blocks) {
   check_cuda_tensor(master, "master");
   check_cuda_tensor(grad, "grad");
   check_cuda_tensor(m, "m");
@@ -169,7 +169,9 @@ void adamw_step(at::Tensor& master, const at::Tensor& grad, at::Tensor& m, at::T
   const float bc1 = static_cast<float>(1.0 - std::pow(beta1, static_cast<double>(step)));
   const float bc2s = static_cast<float>(std::sqrt(1.0 - std::pow(beta2, static_cast<double>(step))));
   c10::cuda::CUDAGuard guard(master.device());
-  const int grid = grid_for((n + 3) / 4);
+  // max_blocks > 0 caps the CTAs (an update running on a side stream next to compute kernels)
+  const int grid = max_blocks > 0 ? std::min<int>(grid_for((n + 3) / 4), static_cast<int>(max_blocks))
+                                  : grid_for((n + 3) / 4);
   auto aligned = [](const void* p, int bytes) { return reinterpret_cast<uintptr_t>(p) % bytes == 0; };
   const bool vec = aligned(master.data_ptr(), 16) && aligned(grad.data_ptr(), 16) && aligned(m.data_ptr(), 16) &&
                    aligned(v.data_ptr(), 16) && (outp == nullptr || aligned(outp, 8));

@@ -61,6 +61,7 @@ struct SaSmem {
   alignas(1024) uint8_t k[SaCfg<D>::kBufs][SaCfg<D>::kAtoms * kKAtom];
   alignas(1024) uint8_t p[SaCfg<D>::kBufs][kKeys * 128];
   uint64_t q_full;
+  uint64_t table_full;  // the producers finished the token's entry table
   uint64_t k_full[SaCfg<D>::kBufs];
   uint64_t k_empty[SaCfg<D>::kBufs];
   uint64_t s_full[2];
@@ -122,18 +123,31 @@ struct SaParams {
 // fixed part): entry j < W is window row win_idx[j] of the raw KV, entry j >= W is compressed row
 // comp_idx[j - W]; -1 marks a masked, negative or out-of-range entry. The gather and the softmax
 // read it instead of the index arrays in global memory.
-__device__ __forceinline__ void build_entries(const SaParams& p, int b, int t, int32_t* ent) {
+__device__ __forceinline__ int32_t entry_of(const SaParams& p, int b, int t, int j) {
   const int64_t tok = static_cast<int64_t>(b) * p.L + t;
-  for (int j = threadIdx.x; j < p.W + p.K; j += blockDim.x) {
-    int32_t e = -1;
-    if (j < p.W) {
-      const int64_t idx = p.win_idx[tok * p.W + j];
-      if (p.win_mask[tok * p.W + j] != 0 && idx >= 0 && idx < p.S) e = static_cast<int32_t>(idx);
-    } else {
-      const int64_t idx = p.comp_idx[tok * p.K + (j - p.W)];
-      if (idx >= 0 && idx < p.C) e = static_cast<int32_t>(idx);
+  if (j < p.W) {
+    const int64_t idx = p.win_idx[tok * p.W + j];
+    return p.win_mask[tok * p.W + j] != 0 && idx >= 0 && idx < p.S ? static_cast<int32_t>(idx) : -1;
+  }
+  const int64_t idx = p.comp_idx[tok * p.K + (j - p.W)];
+  return idx >= 0 && idx < p.C ? static_cast<int32_t>(idx) : -1;
+}
+// The 128 producer threads fill the table; the index loads of up to eight entries per thread are
+// issued before any of them is used, so a token pays about one global-memory latency for it.
+__device__ __forceinline__ void build_table(const SaParams& p, int b, int t, int32_t* ent, int pt) {
+  const int entries = p.W + p.K;
+  for (int base = pt; base < entries; base += 128 * 8) {
+    int32_t e[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = base + u * 128;
+      e[u] = j < entries ? entry_of(p, b, t, j) : -1;
     }
-    ent[j] = e;
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int j = base + u * 128;
+      if (j < entries) ent[j] = e[u];
+    }
   }
 }
 __device__ __forceinline__ int32_t entry_at(const SaParams& p, const int32_t* ent, int j) {
@@ -156,12 +170,12 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_fwd_kernel(const Sa
   const int t = blockIdx.x, b = blockIdx.y, hg = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int entries = p.W + p.K;
-  build_entries(p, b, t, ent);
   const int tiles = (entries + kKeys - 1) / kKeys;
   const int64_t tok = static_cast<int64_t>(b) * p.L + t;
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.q_full, 128);
+    mbar_init(&sm.table_full, 128);
     for (int i = 0; i < kBufs; ++i) {
       mbar_init(&sm.k_full[i], 128);
       mbar_init(&sm.k_empty[i], 1);
@@ -205,6 +219,10 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_fwd_kernel(const Sa
         cp_async16(qbase + (ch >> 3) * kQAtom + swz(row, ch & 7), qsrc + (ok ? row * D + ch * 8 : 0), ok);
       }
       cp_async_commit();
+      // the entry table is built while Q is in flight; the softmax warps wait for it on table_full
+      build_table(p, b, t, ent, pt);
+      mbar_arrive(&sm.table_full);
+      producer_sync();
       cp_async_wait_all();
       fence_proxy_async_smem();
       mbar_arrive(&sm.q_full);
@@ -292,7 +310,10 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_fwd_kernel(const Sa
     // ---------------- softmax (warps 0-3, thread = key row = TMEM lane) ----------------
     const int row = threadIdx.x;  // 0..127
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    for (int it = 0; it < tiles; ++it) {
+    if (!warp_wait(&sm.table_full, 0, p.status, kSaWaitQ)) sm.fail = 1;
+    softmax_sync();
+    failed = sm.fail != 0;
+    for (int it = 0; it < tiles && !failed; ++it) {
       const int buf = it % kBufs;
       if (!warp_wait(&sm.s_full[it & 1], (it >> 1) & 1, p.status, kSaWaitS)) sm.fail = 1;
       softmax_sync();
@@ -479,6 +500,7 @@ struct SbSmem {
   alignas(1024) uint8_t k[SbCfg<D>::kBufs][SbCfg<D>::kHalfAtoms * kKAtom];  // contiguous halves
   alignas(1024) uint8_t ds[kKeys * 128];
   uint64_t qd_full;
+  uint64_t table_full;
   uint64_t k_full[SbCfg<D>::kBufs];
   uint64_t k_empty[SbCfg<D>::kBufs];
   uint64_t s_full, s_free, ds_full, ds_free, dkv_full, dkv_free, dq_full;
@@ -520,7 +542,6 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_bwd_kernel(const Sb
   SbSmem<D>& sm = *reinterpret_cast<SbSmem<D>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   int32_t* ent = reinterpret_cast<int32_t*>(&sm + 1);
   const int t = sp.t0 + blockIdx.x, b = blockIdx.y, hg = blockIdx.z;
-  build_entries(p, b, t, ent);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tiles = (p.W + p.K + kKeys - 1) / kKeys;
   const int64_t tok = static_cast<int64_t>(b) * p.L + t;
@@ -528,6 +549,7 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_bwd_kernel(const Sb
 
   if (threadIdx.x == 0) {
     mbar_init(&sm.qd_full, 128);
+    mbar_init(&sm.table_full, 128);
     for (int i = 0; i < kBufs; ++i) {
       mbar_init(&sm.k_full[i], 128);
       mbar_init(&sm.k_empty[i], 1);
@@ -572,6 +594,9 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_bwd_kernel(const Sb
         cp_async16(db + off, dsrc + (ok ? row * D + ch * 8 : 0), ok);
       }
       cp_async_commit();
+      build_table(p, b, t, ent, pt);
+      mbar_arrive(&sm.table_full);
+      producer_sync();
       cp_async_wait_all();
       fence_proxy_async_smem();
       mbar_arrive(&sm.qd_full);
@@ -736,6 +761,9 @@ __global__ void __launch_bounds__(kSaThreads, 1) sparse_attn_bwd_kernel(const Sb
       softmax_sync();
     }
     bool failed = false;
+    if (!warp_wait(&sm.table_full, 0, p.status, kSbWaitQ)) sm.fail = 1;
+    softmax_sync();
+    failed = sm.fail != 0;
     int g = 0;
     for (int it = 0; it < tiles && !failed; ++it) {
       if (!warp_wait(&sm.s_full, it & 1, p.status, kSbWaitS)) sm.fail = 1;

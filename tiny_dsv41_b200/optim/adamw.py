@@ -33,7 +33,8 @@ _IN_FLIGHT = 4  # side-stream updates the caller's stream may run ahead of
 class FusedAdamW:
     def __init__(self, params, lr: float = 1e-4, betas=(0.9, 0.999), eps: float = 1e-8,
                  weight_decay: float = 0.01, *, moment_dtype: torch.dtype = torch.float32,
-                 in_backward: bool = False, grad_scale: float = 1.0, side_stream: bool = False) -> None:
+                 in_backward: bool = False, grad_scale: float = 1.0, side_stream: bool = False,
+                 side_blocks: int = 0) -> None:
         self.params = [p for p in params if p.requires_grad]
         self.lr, self.betas, self.eps, self.weight_decay = lr, betas, eps, weight_decay
         self.moment_dtype = moment_dtype
@@ -51,6 +52,7 @@ class FusedAdamW:
         device = self.params[0].device if self.params else torch.device("cpu")
         self.stream = torch.cuda.Stream(device=device) if side_stream and device.type == "cuda" else None
         self._inflight: deque = deque()
+        self.side_blocks = side_blocks if self.stream is not None else 0  # CTA cap beside compute (0 = none)
         self._step_t = torch.zeros(1, dtype=torch.int32, device=device) if device.type == "cuda" else None
         self._hooks = []
         self._pending_step = False
@@ -132,7 +134,8 @@ class FusedAdamW:
             out = data if data.dtype == torch.bfloat16 else None
             ext().adamw_step(st["master"], grad.contiguous(), st["m"], st["v"], out, self.lr, beta1, beta2,
                              self.eps, self.weight_decay, self.step_count, self.grad_scale, clip_coefficient,
-                             self._step_t if self._step_t is not None and self._step_t.device == data.device else None)
+                             self._step_t if self._step_t is not None and self._step_t.device == data.device else None,
+                             self.side_blocks)
             if out is None:
                 data.copy_(st["master"])
             return

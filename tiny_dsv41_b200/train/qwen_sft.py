@@ -93,7 +93,10 @@ class QwenTrainer:
         # device status word (bounded peer waits, bounds checks) read once per step by the loops
         self.monitor = StatusMonitor(rt.device)
         hyper = dict(lr=lr, betas=(0.9, 0.95), weight_decay=0.1, moment_dtype=moment_dtype)
-        side = rt.device.type == "cuda"
+        # in-backward updates on side streams (TDSV_SIDE_STREAM=0 keeps them on the compute stream;
+        # TDSV_SIDE_BLOCKS caps the CTAs of the expert update running beside the backward GEMMs)
+        side = rt.device.type == "cuda" and os.environ.get("TDSV_SIDE_STREAM", "1") != "0"
+        side_blocks = int(os.environ.get("TDSV_SIDE_BLOCKS", "0"))
         if self.dense_sync == "peer":
             from ..parallel.peer_fsdp import PeerShardedOptimizer, decoder_units
 
@@ -104,7 +107,8 @@ class QwenTrainer:
             dense_opt = FusedAdamW(dense, in_backward=True, side_stream=side and self.dense_sync != "fsdp", **hyper)
         self.optimizers = [
             dense_opt,
-            FusedAdamW(self.expert_params, in_backward=True, grad_scale=1.0 / self.world, side_stream=side, **hyper),
+            FusedAdamW(self.expert_params, in_backward=True, grad_scale=1.0 / self.world, side_stream=side,
+                       side_blocks=side_blocks, **hyper),
         ]
         # CUDA graph of a whole training step (forward, backward, in-backward optimizer, NVLink
         # exchanges): captured after `graph_warmup` eager steps, then replayed. Every per-step value a
