@@ -83,3 +83,40 @@ def test_kv_cache_decoding_gpu():
             assert _rel(a, b) < 2e-2
             ids.append(int(b.argmax()))
     assert inc.prefills == 1
+
+
+def test_checkpoint_recompute_reuses_attention_and_matches_plain_backward():
+    """With gradient checkpointing the recompute reuses the first pass's attention output
+    (parallel/replay.py); the gradients must equal those of the same model without checkpointing."""
+    torch.manual_seed(3)
+    cfg = Qwen3MoeConfig.tiny(num_hidden_layers=2, vocab_size=512)
+    plain = Qwen3MoeForCausalLM(cfg).cuda().to(torch.bfloat16)
+    ckpt = Qwen3MoeForCausalLM(cfg).cuda().to(torch.bfloat16)
+    ckpt.load_state_dict(plain.state_dict())
+    ckpt.gradient_checkpointing_enable()
+    ids = torch.randint(0, 512, (1, 256), device="cuda")
+    calls = {"n": 0}
+    a = plain(ids, labels=ids, output_router_logits=True)
+    a.loss.backward()
+    from tiny_dsv41_b200.ops import _ext
+
+    module = _ext._ext
+    original = module.attn_fwd
+
+    def counting(*args):
+        calls["n"] += 1
+        return original(*args)
+
+    try:
+        _ext._ext = type("Wrapped", (), {"__getattr__": lambda self, n: counting if n == "attn_fwd"
+                                         else getattr(module, n)})()
+        b = ckpt(ids, labels=ids, output_router_logits=True)
+        b.loss.backward()
+    finally:
+        _ext._ext = module
+    assert calls["n"] == cfg.num_hidden_layers  # forward only: the recompute ran no attention kernel
+    assert abs(a.loss.item() - b.loss.item()) < 1e-3
+    grads = dict(plain.named_parameters())
+    for name, p in ckpt.named_parameters():
+        err = _rel(p.grad, grads[name].grad)
+        assert err < 2e-2, (name, err)

@@ -4,7 +4,8 @@
 Layout: q [B, L, Hq, D], k/v [B, L, Hkv, D] (the token-major layout the QKV kernel writes).
 On CUDA, the plain causal case (no extra mask, no dropout, bf16, head dim 128, L a multiple of
 128) runs this library's tcgen05 flash-attention kernels (``csrc/attention.cu``): forward
-saves (out, lse), backward recomputes P per tile. Anything else (an explicit mask for padding,
+saves (out, lse), backward recomputes P per tile; under activation checkpointing the recompute
+reuses the first pass's (out, lse) (``parallel/replay.py``) instead of running the forward again. Anything else (an explicit mask for padding,
 context parallelism or a KV cache; dropout; other shapes) runs PyTorch's scaled-dot-product
 attention, as do CPU tensors (the numerical oracle).
 """
@@ -20,7 +21,16 @@ from ._ext import ext, on_gpu
 class _FlashAttention(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v):
-        out, lse = ext().attn_fwd(q, k, v)
+        from ..parallel import replay
+
+        handle, mode = replay.current()
+        if mode == "replay":  # checkpoint recompute: the first pass's result (same inputs, same kernel)
+            out, lse = handle.next_attention()
+            out = out.clone()  # a fresh output: the record must not become this node's output
+        else:
+            out, lse = ext().attn_fwd(q, k, v)
+            if mode == "record":
+                handle.record_attention((out.detach(), lse))
         ctx.save_for_backward(q, k, v, out, lse)
         return out
 

@@ -5,7 +5,9 @@ again (recompute) during backward. Re-running the MoE token exchange would move 
 over NVLink a second time. Instead, the first pass records what its exchanges produced (the
 received expert-major rows and the combined output, plus the routing state), and the recompute
 replays them: the recomputed graph gets the same tensors without any transfer, and its backward
-still runs the real reverse exchanges.
+still runs the real reverse exchanges. The causal attention forward is treated the same way: its
+output and log-sum-exp (34 MB per layer at L 4096) are kept from the first pass, so the
+recompute runs no attention kernel.
 
 ``checkpoint_contexts`` is passed as ``context_fn`` to ``torch.utils.checkpoint.checkpoint``
 (non-reentrant): each checkpointed call gets one ``ReplayHandle``; the forward runs under its
@@ -24,6 +26,20 @@ class ReplayHandle:
     def __init__(self) -> None:
         self.items: list = []
         self.cursor = 0
+        # attention outputs (out, lse) of the first pass: the recompute reuses them instead of
+        # running the attention forward again (its backward still gets recomputed q / k / v)
+        self.attention: list = []
+        self.attention_cursor = 0
+
+    def record_attention(self, item) -> None:
+        self.attention.append(item)
+
+    def next_attention(self):
+        if self.attention_cursor >= len(self.attention):
+            raise RuntimeError("recompute ran more attention calls than the recorded forward")
+        item = self.attention[self.attention_cursor]
+        self.attention_cursor += 1
+        return item
 
     def record(self, item) -> None:
         self.items.append(item)
@@ -43,6 +59,7 @@ class _Mode:
     def __enter__(self):
         if self.mode == "replay":
             self.handle.cursor = 0
+            self.handle.attention_cursor = 0
         stack = getattr(_local, "stack", None)
         if stack is None:
             stack = _local.stack = []
