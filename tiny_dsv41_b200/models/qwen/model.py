@@ -70,7 +70,7 @@ class Qwen3MoeAttention(nn.Module):
                                       ops.inv_freq(self.head_dim, self.rope_theta), hidden.device)
         if fusable(self.q_proj, self.k_proj, self.v_proj):
             weight = torch.cat((self.q_proj.weight, self.k_proj.weight, self.v_proj.weight), dim=0)
-            qkv = ops.linear(hidden, weight)
+            qkv = ops.linear(hidden, weight, replayable=True)  # the recompute reuses this product
         else:
             qkv = torch.cat((self.q_proj(hidden), self.k_proj(hidden), self.v_proj(hidden)), dim=-1)
         q, k, v = ops.qk_norm_rope(qkv, self.q_norm.weight, self.k_norm.weight, position_ids, freqs,
@@ -104,6 +104,8 @@ class Qwen3MoeAttention(nn.Module):
             causal = torch.ones(length, length, dtype=torch.bool, device=hidden.device).tril()
             mask = causal.view(1, 1, length, length) & attention_mask.bool()[:, None, None, :]
         out = ops.causal_attention(q, k, v, mask=mask, dropout=self.dropout if self.training else 0.0)
+        if fusable(self.o_proj):
+            return ops.linear(out.reshape(batch, length, -1), self.o_proj.weight, replayable=True)
         return self.o_proj(out.reshape(batch, length, -1))
 
 

@@ -28,11 +28,21 @@ def matmul_nt(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16) -> tor
 
 class _Linear(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, weight):
+    def forward(ctx, x, weight, replayable=False):
         shape = x.shape
         x2 = x.reshape(-1, shape[-1]).contiguous()
-        out = torch.empty(x2.shape[0], weight.shape[0], dtype=torch.bfloat16, device=x.device)
-        ext().gemm(x2, weight, out, False, False, False)
+        handle, mode = (None, None)
+        if replayable:
+            from ..parallel import replay
+
+            handle, mode = replay.current()
+        if mode == "replay":  # checkpoint recompute: the first pass's product of the same operands
+            out = handle.next_attention().clone()
+        else:
+            out = torch.empty(x2.shape[0], weight.shape[0], dtype=torch.bfloat16, device=x.device)
+            ext().gemm(x2, weight, out, False, False, False)
+            if mode == "record":
+                handle.record_attention(out.detach())
         ctx.save_for_backward(x2, weight)
         ctx.shape = shape
         return out.view(*shape[:-1], weight.shape[0])
@@ -49,12 +59,15 @@ class _Linear(torch.autograd.Function):
         if ctx.needs_input_grad[1]:
             dw = torch.empty_like(weight)
             ext().gemm(dy2, x2, dw, True, True, False)
-        return dx, dw
+        return dx, dw, None
 
 
-def linear(x: torch.Tensor, weight: torch.Tensor) -> torch.Tensor:
+def linear(x: torch.Tensor, weight: torch.Tensor, *, replayable: bool = False) -> torch.Tensor:
+    """``x @ weight.T``. ``replayable``: under activation checkpointing the recompute reuses the
+    first pass's product (kept by ``parallel/replay.py``) instead of running the GEMM again - for
+    small outputs whose recompute costs more than the memory to keep them."""
     if on_gpu(x) and _kernel_ok(x, weight) and weight.shape[0] % 8 == 0 and weight.shape[1] % 8 == 0:
-        return _Linear.apply(x, weight)
+        return _Linear.apply(x, weight, replayable)
     return torch.nn.functional.linear(x, weight.to(x.dtype))
 
 

@@ -55,9 +55,17 @@ def qk_norm_rope_reference(qkv, wq, wk, positions, freqs, hq, hkv, eps):
 class _QKNormRope(torch.autograd.Function):
     @staticmethod
     def forward(ctx, qkv, wq, wk, positions, freqs, hq, hkv, eps):
+        from ..parallel import replay
+
         qkv2 = qkv.reshape(-1, qkv.shape[-1]).contiguous()
         pos = positions.reshape(-1).contiguous()
-        q, k = ext().qk_norm_rope_fwd(qkv2, wq.contiguous(), wk.contiguous(), pos, freqs, hq, hkv, float(eps))
+        handle, mode = replay.current()
+        if mode == "replay":  # checkpoint recompute: the first pass's q / k (same inputs)
+            q, k = (t.clone() for t in handle.next_attention())
+        else:
+            q, k = ext().qk_norm_rope_fwd(qkv2, wq.contiguous(), wk.contiguous(), pos, freqs, hq, hkv, float(eps))
+            if mode == "record":
+                handle.record_attention((q.detach(), k.detach()))
         ctx.save_for_backward(qkv2, wq, wk, pos, freqs)
         ctx.meta = (hq, hkv, eps, qkv.shape)
         v = qkv2[:, (hq + hkv) * 128:].view(-1, hkv, 128)

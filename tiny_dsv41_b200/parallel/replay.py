@@ -5,9 +5,12 @@ again (recompute) during backward. Re-running the MoE token exchange would move 
 over NVLink a second time. Instead, the first pass records what its exchanges produced (the
 received expert-major rows and the combined output, plus the routing state), and the recompute
 replays them: the recomputed graph gets the same tensors without any transfer, and its backward
-still runs the real reverse exchanges. The causal attention forward is treated the same way: its
-output and log-sum-exp (34 MB per layer at L 4096) are kept from the first pass, so the
-recompute runs no attention kernel.
+still runs the real reverse exchanges. The causal attention forward and the small dense
+projections around it (QKV and output, ``ops.linear(..., replayable=True)``) and the per-head
+q / k norm + RoPE are treated the same way: their outputs (about 130 MB per layer at L 4096 for
+Qwen3-30B-A3B) are kept from the first pass, so the recompute runs neither the attention kernel
+nor those GEMMs nor the norm / rotation. Records are consumed in
+the order they were made, so every recorded call must run in the same order in the recompute.
 
 ``checkpoint_contexts`` is passed as ``context_fn`` to ``torch.utils.checkpoint.checkpoint``
 (non-reentrant): each checkpointed call gets one ``ReplayHandle``; the forward runs under its
