@@ -175,6 +175,26 @@ def cases():
                           0.95, 1e-8, 0.1, epoch[0], 1.0, None, None, blocks)
         return step, None, None, n * (2 + 2 + 8 + 2 * 2 * moments.itemsize)
 
+    def fp4_grouped(kind, experts=48, per=512, n=4608, k=5120):
+        # frozen MXFP4 experts at DSV4-Flash gate_up shapes for one EP8 rank (384 / 8 experts,
+        # 4096 tokens x top-6 / 48 = 512 rows each), weight W [n, k] packed along k. The
+        # comparison is the former path, which expanded the codes to a bf16 weight in HBM and ran
+        # the bf16 grouped GEMM.
+        rows_n, cols = (n, k) if kind == "fwd" else (k, n)  # output columns, contraction (dx reads W N-major)
+        codes = torch.randint(0, 256, (experts, n, k // 2), device=dev, dtype=torch.uint8)
+        scales = torch.randint(118, 130, (experts, n, k // 32), device=dev, dtype=torch.uint8)
+        x = torch.randn(experts * per, cols, device=dev, dtype=bf)
+        out = torch.empty(experts * per, rows_n, device=dev, dtype=bf)
+        off = (torch.arange(experts, device=dev, dtype=torch.int32) * per).contiguous()
+        cnt = torch.full((experts,), per, device=dev, dtype=torch.int32)
+        b_mn = kind == "dx"
+
+        def expand_then_gemm():
+            w = C.fp4_dequant(codes, scales)
+            C.grouped_gemm_m(x, w, off, cnt, out, b_mn, x.shape[0])
+        return ((lambda: C.fp4_grouped_gemm(x, codes, scales, off, cnt, out, b_mn, x.shape[0])), expand_then_gemm,
+                2 * experts * per * n * k, None)
+
     return {
         "peer_update": peer_update,
         "sparse_attn_fwd": lambda: sparse_attention("fwd"),
@@ -185,6 +205,8 @@ def cases():
         "grouped_fwd": lambda: grouped("fwd"),
         "grouped_dx": lambda: grouped("dx"),
         "grouped_dw": lambda: grouped("dw"),
+        "fp4_grouped_fwd": lambda: fp4_grouped("fwd"),
+        "fp4_grouped_dx": lambda: fp4_grouped("dx"),
         "adamw": adamw,
         "swiglu": swiglu,
         "rmsnorm": rmsnorm,
@@ -221,7 +243,7 @@ def main(argv=None) -> None:
         if ref is not None:
             rms = _time(ref, args.iters)
             label = ("cudnn_sdpa" if name.startswith("attn") else "gathered_torch" if name.startswith("sparse")
-                     else "cublas")
+                     else "expand_then_gemm" if name.startswith("fp4") else "cublas")
             row.update({f"{label}_ms": round(rms, 4), f"{label}_tflops": round(flops / rms / 1e9, 1)})
         row["peak_source"] = peaks["source"]
         print(json.dumps(row), flush=True)

@@ -41,6 +41,9 @@ std::vector<at::Tensor> moe_route_plan(const at::Tensor& ids, int64_t num_expert
                                        const c10::optional<at::Tensor>& slab_counts, int64_t slab);
 std::vector<at::Tensor> ep_dest_plan(const at::Tensor& ids, int64_t experts_per_rank, int64_t ranks);
 at::Tensor fp4_dequant(const at::Tensor& packed, const at::Tensor& scale);
+void fp4_grouped_gemm(const at::Tensor& a, const at::Tensor& codes, const at::Tensor& scales,
+                      const at::Tensor& group_off, const at::Tensor& group_rows, at::Tensor& out, bool b_mn,
+                      int64_t max_rows);
 std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const at::Tensor& w, double eps);
 std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
                                     const at::Tensor& rstd, bool need_dw);
@@ -184,6 +187,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("cache_fake_quant", &tdsv::cache_fake_quant, "FP8 / FP4 block fake quantization (0 fp8, 1 fp4_index, 2 fp4_kv)");
   m.def("index_scores", &tdsv::index_scores, "DSV4 sparse-indexer scores (tcgen05, fused relu / head reduction)");
   m.def("fp4_dequant", &tdsv::fp4_dequant, "MXFP4 (E2M1 + E8M0 per 32) to bf16");
+  m.def("fp4_grouped_gemm", &tdsv::fp4_grouped_gemm, "expert-grouped GEMM against packed MXFP4 weights");
   m.def("rmsnorm_fwd", &tdsv::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &tdsv::rmsnorm_bwd);
   m.def("column_sum", &tdsv::column_sum);

@@ -377,6 +377,65 @@ def test_frozen_fp4_grouped_linear_grad():
     assert _rel(x.grad, xr.grad) < 1e-2
 
 
+def test_fp4_grouped_gemm_converts_codes_exactly():
+    """A one-hot activation picks single weight values out of the packed GEMM, so every E2M1 code
+    times every E8M0 scale in range must come back bit-exact (forward: K-major weight tiles; input
+    gradient: N-major tiles)."""
+    from tiny_dsv41_b200.ops.fp4 import dequantize_fp4
+
+    torch.manual_seed(16)
+    n, k = 384, 128
+    codes = torch.randint(0, 256, (1, n, k // 2), dtype=torch.uint8)
+    scales = torch.randint(2, 251, (1, n, k // 32), dtype=torch.uint8)
+    want = dequantize_fp4(codes, scales)[0]  # CPU restatement, [n, k]
+    codes, scales = codes.to(DEV), scales.to(DEV)
+    off = torch.zeros(1, device=DEV, dtype=torch.int32)
+    rows = torch.full((1,), 128, device=DEV, dtype=torch.int32)
+    eye = torch.eye(128, k, device=DEV, dtype=torch.bfloat16)
+    out = torch.empty(128, n, device=DEV, dtype=torch.bfloat16)
+    ops.ext().fp4_grouped_gemm(eye, codes, scales, off, rows, out, False, 128)
+    assert torch.equal(out.cpu(), want.t()[:128])
+    # input gradient: codes [G, K = n, N = k] read N-major; a one-hot dy row picks weight row r
+    dy = torch.eye(128, n, device=DEV, dtype=torch.bfloat16)
+    dx = torch.empty(128, k, device=DEV, dtype=torch.bfloat16)
+    ops.ext().fp4_grouped_gemm(dy, codes, scales, off, rows, dx, True, 128)
+    assert torch.equal(dx.cpu(), want[:128])
+
+
+@pytest.mark.parametrize("n,k", [(384, 256), (192, 320), (2048, 512)])
+def test_fp4_grouped_gemm_ragged_groups(n, k, monkeypatch):
+    """Uneven and empty expert groups, an N tail inside a tile, both tile widths; the packed path
+    never expands the weight (the dequantisation kernel is not called)."""
+    from tiny_dsv41_b200.ops import fp4 as F4
+    from tiny_dsv41_b200.utils.quant import quantize_fp4_rows
+
+    torch.manual_seed(17)
+    sizes = [256, 0, 128, 384, 128]
+    e = len(sizes)
+    packed, scale = quantize_fp4_rows(torch.randn(e * n, k) * 0.05)
+    codes = packed.view(torch.uint8).view(e, n, k // 2).to(DEV)
+    scales = scale.view(torch.uint8).view(e, n, k // 32).to(DEV)
+    w = F4.dequantize_fp4(codes, scales).float()
+    starts = [sum(sizes[:i]) for i in range(e)]
+    total = sum(sizes)
+    x = torch.randn(total, k, device=DEV, dtype=torch.bfloat16, requires_grad=True)
+    off = torch.tensor(starts, device=DEV, dtype=torch.int32)
+    rows = torch.tensor(sizes, device=DEV, dtype=torch.int32)
+
+    def no_expansion(*_):
+        raise AssertionError("the packed GEMM expanded the weight")
+
+    monkeypatch.setattr(F4, "dequantize_fp4", no_expansion)
+    y = F4.fp4_grouped_linear(x, codes, scales, off, rows, n)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr = x.detach().float().requires_grad_()
+    yr = torch.cat([xr[s0:s0 + c] @ w[i].t() for i, (s0, c) in enumerate(zip(starts, sizes))])
+    yr.backward(g.float())
+    assert _rel(y, yr) < 1e-2
+    assert _rel(x.grad, xr.grad) < 1e-2
+
+
 def test_bitwise_determinism_30_runs():
     """Fixed-order reductions: repeated launches give identical bits (combine, RMSNorm weight
     gradient, grouped weight-gradient GEMM, routing plan)."""

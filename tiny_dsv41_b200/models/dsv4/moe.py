@@ -64,8 +64,9 @@ class RoutedExperts(nn.Module):
 
     def freeze_fp4(self, gate_up_fp4, gate_up_scale, down_fp4, down_scale) -> None:
         """Replace the bf16 expert weights by frozen MXFP4 codes and E8M0 scales (uint8):
-        gate_up [E, I, 2, H/2] / [E, I, 2, H/32], down [E, H, I/2] / [E, H, I/32]. The weights
-        are expanded per GEMM and never trained (LoRA SFT over a released FP4 checkpoint)."""
+        gate_up [E, I, 2, H/2] / [E, I, 2, H/32], down [E, H, I/2] / [E, H, I/32]. The grouped
+        GEMMs read them packed and they are never trained (LoRA SFT over a released FP4
+        checkpoint)."""
         e, i, h = self.num_experts, self.intermediate, self.hidden_size
         shapes = ((gate_up_fp4, (e, i, 2, h // 2)), (gate_up_scale, (e, i, 2, h // 32)),
                   (down_fp4, (e, h, i // 2)), (down_scale, (e, h, i // 32)))
