@@ -67,7 +67,10 @@ def cases():
         flops = 2 * rows * 2 * inter * h
         if kind == "fwd":
             out = torch.empty(rows, 2 * inter, device=dev, dtype=bf)
-            return (lambda: C.grouped_gemm_m(x, w1, off, size, out, False, rows)), None, flops, None
+            ends = torch.cumsum(size, 0, dtype=torch.int32)
+            w1t = w1.transpose(1, 2)
+            return ((lambda: C.grouped_gemm_m(x, w1, off, size, out, False, rows)),
+                    (lambda: torch._grouped_mm(x, w1t, offs=ends)), flops, None)
         if kind == "dx":
             out = torch.empty(rows, h, device=dev, dtype=bf)
             return (lambda: C.grouped_gemm_m(gu, w1, off, size, out, True, rows)), None, flops, None
@@ -205,6 +208,10 @@ def cases():
         "grouped_fwd": lambda: grouped("fwd"),
         "grouped_dx": lambda: grouped("dx"),
         "grouped_dw": lambda: grouped("dw"),
+        # the Qwen3-30B-A3B step at EP2: 4096 tokens x top-8 per rank over 64 local experts
+        "step_grouped_fwd": lambda: grouped("fwd", experts=64, per=512),
+        "step_grouped_dx": lambda: grouped("dx", experts=64, per=512),
+        "step_grouped_dw": lambda: grouped("dw", experts=64, per=512),
         "fp4_grouped_fwd": lambda: fp4_grouped("fwd"),
         "fp4_grouped_dx": lambda: fp4_grouped("dx"),
         "adamw": adamw,
@@ -243,7 +250,8 @@ def main(argv=None) -> None:
         if ref is not None:
             rms = _time(ref, args.iters)
             label = ("cudnn_sdpa" if name.startswith("attn") else "gathered_torch" if name.startswith("sparse")
-                     else "expand_then_gemm" if name.startswith("fp4") else "cublas")
+                     else "expand_then_gemm" if name.startswith("fp4")
+                     else "torch_grouped_mm" if "grouped" in name else "cublas")
             row.update({f"{label}_ms": round(rms, 4), f"{label}_tflops": round(flops / rms / 1e9, 1)})
         row["peak_source"] = peaks["source"]
         print(json.dumps(row), flush=True)
