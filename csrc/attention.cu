@@ -6,7 +6,9 @@
 // contraction is a tcgen05.mma with its fp32 accumulator in tensor memory, and every mbarrier wait
 // is bounded (a timeout records a status code and the CTA drains instead of spinning forever).
 //
-// Forward: one CTA per (128-query tile, head, batch), 320 threads.
+// Forward, GQA groups of even size (the Qwen shapes): attn_fwd2_kernel, one CTA per (128-query
+// tile, pair of query heads of one key / value head, batch); see its own comment below.
+// Forward, other group sizes (and the traced diagnostic): one CTA per (128-query tile, head, batch), 320 threads.
 //   warp 0     TMA producer: Q once, then K_j / V_j tiles through a two-stage ring
 //   warp 1     MMA issuer: S_{j+1} = Q K_{j+1}^T is issued before P_j is ready, so the next score
 //              tile overlaps the softmax of this one (S is double-buffered in tensor memory)
@@ -102,6 +104,7 @@ struct FwdSmem {
   uint64_t s_free[2];
   uint64_t p_full;
   uint64_t pv_done;
+  uint64_t o_ready;  // the last PV has completed (committed once)
   uint64_t pair[4];
   float xchg[2][2][kTile];  // [iteration parity][half][row]: partial maxima, then partial sums
   uint32_t tmem_base;
@@ -143,6 +146,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
     }
     mbar_init(&sm.p_full, 256);
     mbar_init(&sm.pv_done, 1);
+    mbar_init(&sm.o_ready, 1);
     for (int qd = 0; qd < 4; ++qd) mbar_init(&sm.pair[qd], 64);
     fence_barrier_init();
   }
@@ -225,6 +229,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
                       mnmajor_desc(va, kk, kAtom), idesc_pv, (j > 0 || kk > 0));
         umma_commit(&sm.pv_done);
         umma_commit(&sm.v_empty[j & 1]);
+        if (j == n_kv - 1) umma_commit(&sm.o_ready);
         TDSV_TRACE(4, j);
       }
     }
@@ -342,7 +347,9 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
       mbar_arrive(&sm.pair[quarter]);
       ok = warp_wait(&sm.pair[quarter], n_kv & 1, status, kFwdWaitPair);
     }
-    if (ok && warp_wait(&sm.pv_done, (n_kv - 1) & 1, status, kFwdWaitLast)) {
+    // a dedicated barrier for the final O: a parity wait on pv_done could see phase n_kv - 1 as
+    // complete while PV_n_kv-2 is still pending
+    if (ok && warp_wait(&sm.o_ready, 0, status, kFwdWaitLast)) {
       tc_fence_after();
       const float l_row = sm.xchg[n_kv & 1][0][r] + sm.xchg[n_kv & 1][1][r];
       const float inv = 1.f / l_row;
@@ -363,6 +370,259 @@ __global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd_kernel(const __grid_c
       if (half == 0)
         lse[(static_cast<int64_t>(b) * heads + h) * seq + qi * kTile + r] =
             (m_used + log2f(l_row)) * 0.69314718055994531f;
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------
+// Forward, two query heads per CTA (GQA groups of even size): heads 2p and 2p + 1 of one key /
+// value head share every K / V tile, so the tensor cores compute one head's scores or PV while
+// the other head's softmax runs (two softmax warpgroups in ping-pong), and each CTA issues half
+// the TMA traffic per query tile.
+//   warp 0     TMA producer: both Q tiles once, then 64-key K_j / V_j tiles through a 4-stage ring
+//   warp 1     MMA issuer. Iteration j: PV_t,j = P_t,j V_j for t = 0, 1 as each P arrives, then
+//              S_t,j+2 = Q_t K_j+2^T into the buffer PV_t,j has just finished reading
+//   warps 2-5  softmax of head 2p, warps 6-9 of head 2p + 1: one thread per query row and 64 keys
+//              per iteration; the running maximum is raised only when it grows by more than 2^8
+//              (O rescaled in TMEM then); P (bf16) overwrites the first 32 columns of its own S
+//              buffer and the PV MMA reads it from there as its A operand.
+//   TMEM (512 columns): head t at 256 t: S buffers [0, 64) and [64, 128), O [128, 256).
+//   Q stays in shared memory (A operand of the S MMAs).
+constexpr int kKeys2 = 64;     // keys per iteration
+constexpr int kKvStages2 = 4;  // K / V ring depth
+struct Fwd2Smem {
+  alignas(1024) uint8_t q[2][2 * kAtom];
+  alignas(1024) uint8_t k[kKvStages2][2 * kHalfAtom];
+  alignas(1024) uint8_t v[kKvStages2][2 * kHalfAtom];
+  uint64_t q_full;
+  uint64_t k_full[kKvStages2];
+  uint64_t k_empty[kKvStages2];
+  uint64_t v_full[kKvStages2];
+  uint64_t v_empty[kKvStages2];
+  uint64_t s_full[2][2];   // [head][buffer]
+  uint64_t p_full[2][2];   // [head][buffer]
+  uint64_t pv_done[2];     // [head]
+  uint64_t o_ready[2];     // [head]: the last PV has completed (committed once)
+  uint32_t tmem_base;
+};
+
+__global__ void __launch_bounds__(kFwdThreads, 1) attn_fwd2_kernel(const __grid_constant__ CUtensorMap tq,
+                                                           const __grid_constant__ KvMaps kv,
+                                                           __nv_bfloat16* __restrict__ out, float* __restrict__ lse,
+                                                           int seq, int heads, int kv_heads, float scale_log2,
+                                                           int* __restrict__ status) {
+  extern __shared__ uint8_t smem_raw[];
+  Fwd2Smem& sm = *reinterpret_cast<Fwd2Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_q = seq / kTile;
+  const int h0 = 2 * static_cast<int>(blockIdx.x);
+  const int qi = n_q - 1 - static_cast<int>(blockIdx.y);  // longest causal rows in the first wave
+  const int b = blockIdx.z;
+  const int hk = h0 / (heads / kv_heads);
+  const int gq = kv.q_offset / kTile + qi;  // keys [0, (gq + 1) * 128) are visible
+  const int n_it = 2 * (gq + 1);            // 64-key iterations
+  const int row0 = b * seq + qi * kTile;
+  // 64-key tile j of the global key order: its owner and first row in that owner's tensors
+  auto key_owner = [&](int j) { return j * kKeys2 / kv.chunk; };
+  auto key_row = [&](int j) { return b * kv.chunk + j * kKeys2 - key_owner(j) * kv.chunk; };
+
+  if (threadIdx.x == 0) {
+    mbar_init(&sm.q_full, 1);
+    for (int s = 0; s < kKvStages2; ++s) {
+      mbar_init(&sm.k_full[s], 1);
+      mbar_init(&sm.k_empty[s], 1);
+      mbar_init(&sm.v_full[s], 1);
+      mbar_init(&sm.v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; ++t) {
+      for (int u = 0; u < 2; ++u) {
+        mbar_init(&sm.s_full[t][u], 1);
+        mbar_init(&sm.p_full[t][u], 128);
+      }
+      mbar_init(&sm.pv_done[t], 1);
+      mbar_init(&sm.o_ready[t], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&sm.tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tq);
+      mbar_arrive_expect_tx(&sm.q_full, 4 * kAtom);
+      for (int t = 0; t < 2; ++t) {
+        tma_load_3d(sm.q[t], &tq, &sm.q_full, 0, h0 + t, row0);
+        tma_load_3d(sm.q[t] + kAtom, &tq, &sm.q_full, 64, h0 + t, row0);
+      }
+      for (int j = 0; j < n_it; ++j) {
+        const int s = j % kKvStages2;
+        const uint32_t ph = ((j / kKvStages2) & 1) ^ 1;
+        const int owner = key_owner(j), key0 = key_row(j);
+        if (!mbar_sleep_wait(&sm.k_empty[s], ph, status, kFwdWaitKvEmpty)) break;
+        mbar_arrive_expect_tx(&sm.k_full[s], 2 * kHalfAtom);
+        tma_load_3d(sm.k[s], &kv.k[owner], &sm.k_full[s], 0, hk, key0);
+        tma_load_3d(sm.k[s] + kHalfAtom, &kv.k[owner], &sm.k_full[s], 64, hk, key0);
+        if (!mbar_sleep_wait(&sm.v_empty[s], ph, status, kFwdWaitKvEmpty)) break;
+        mbar_arrive_expect_tx(&sm.v_full[s], 2 * kHalfAtom);
+        tma_load_3d(sm.v[s], &kv.v[owner], &sm.v_full[s], 0, hk, key0);
+        tma_load_3d(sm.v[s] + kHalfAtom, &kv.v[owner], &sm.v_full[s], 64, hk, key0);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(kTile, kKeys2, false, false);
+      constexpr uint32_t idesc_pv = make_idesc_bf16(kTile, kDim, false, true);
+      // S_t,j into buffer j & 1 of head t
+      auto issue_s = [&](int t, int j) {
+        const uint32_t qa = smem_u32(sm.q[t]), ka = smem_u32(sm.k[j % kKvStages2]);
+#pragma unroll
+        for (int kk = 0; kk < kDim / 16; ++kk)
+          umma_f16(tmem + t * 256 + (j & 1) * kKeys2, kmajor_desc(qa, kk, kAtom), kmajor_desc(ka, kk, kHalfAtom),
+                   idesc_s, kk > 0);
+        umma_commit(&sm.s_full[t][j & 1]);
+        if (t == 1) umma_commit(&sm.k_empty[j % kKvStages2]);
+      };
+      bool ok = mbar_sleep_wait(&sm.q_full, 0, status, kFwdWaitQ);
+      for (int j = 0; ok && j < 2; ++j) {
+        if (!(ok = mbar_sleep_wait(&sm.k_full[j], 0, status, kFwdWaitKv0))) break;
+        tc_fence_after();
+        issue_s(0, j);
+        issue_s(1, j);
+      }
+      for (int j = 0; ok && j < n_it; ++j) {
+        const int s = j % kKvStages2;
+        for (int t = 0; t < 2; ++t) {
+          if (!(ok = mbar_sleep_wait(&sm.p_full[t][j & 1], (j >> 1) & 1, status, kFwdWaitP))) break;
+          if (t == 0 && !(ok = mbar_sleep_wait(&sm.v_full[s], (j / kKvStages2) & 1, status, kFwdWaitKv))) break;
+          tc_fence_after();
+          const uint32_t va = smem_u32(sm.v[s]);
+#pragma unroll
+          for (int kk = 0; kk < kKeys2 / 16; ++kk)
+            umma_f16_ts(tmem + t * 256 + 2 * kKeys2, tmem + t * 256 + (j & 1) * kKeys2 + kk * 8,
+                        mnmajor_desc(va, kk, kHalfAtom), idesc_pv, (j > 0 || kk > 0));
+          umma_commit(&sm.pv_done[t]);
+          if (t == 1) umma_commit(&sm.v_empty[s]);
+          if (j == n_it - 1) umma_commit(&sm.o_ready[t]);
+        }
+        if (!ok || j + 2 >= n_it) continue;
+        // S_t,j+2 goes into the buffer that P_t,j occupies: it waits for PV_t,j to complete
+        const int s2 = (j + 2) % kKvStages2;
+        if (!(ok = mbar_sleep_wait(&sm.k_full[s2], ((j + 2) / kKvStages2) & 1, status, kFwdWaitKv))) break;
+        for (int t = 0; t < 2; ++t) {
+          if (!(ok = mbar_sleep_wait(&sm.pv_done[t], j & 1, status, kFwdWaitSFree))) break;
+          tc_fence_after();
+          issue_s(t, j + 2);
+        }
+      }
+    }
+  } else {
+    // softmax: warps 2-5 own head h0, warps 6-9 head h0 + 1; thread <-> query row r (TMEM lane)
+    const int t = (warp - 2) >> 2, quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_addr = tmem + t * 256 + (static_cast<uint32_t>(quarter * 32) << 16);
+    const int q_pos = gq * kTile + r;  // global position (keys are numbered globally too)
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; ok && j < n_it; ++j) {
+      const int buf = j & 1;
+      if (!(ok = warp_wait(&sm.s_full[t][buf], (j >> 1) & 1, status, kFwdWaitS))) break;
+      tc_fence_after();
+      uint32_t sv[2][32];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) tmem_ld_32x32b_x32(lane_addr + buf * kKeys2 + c * 32, sv[c]);
+      tmem_ld_wait();
+      const int key0 = j * kKeys2;
+      if (key0 + kKeys2 - 1 > q_pos) {  // the causal diagonal crosses this tile for this row
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (key0 + c * 32 + i > q_pos) sv[c][i] = __float_as_uint(-INFINITY);
+      }
+      float m8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) m8[i] = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) m8[i & 7] = fmaxf(m8[i & 7], __uint_as_float(sv[c][i]));
+      const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * scale_log2;
+      float alpha = 1.f;
+      if (mx > m_used + 8.f) {  // raise the reference maximum only when it grows by more than 2^8
+        alpha = (m_used == -INFINITY) ? 0.f : ex2_approx(m_used - mx);
+        m_used = mx;
+      }
+      float s8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s8[i] = 0.f;
+      uint32_t packed[32];
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = ex2_approx(fmaf(__uint_as_float(sv[c][i]), scale_log2, -m_used));
+          const float p1 = ex2_approx(fmaf(__uint_as_float(sv[c][i + 1]), scale_log2, -m_used));
+          const __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
+          s8[(i >> 1) & 7] += p0 + p1;
+          packed[c * 16 + i / 2] = *reinterpret_cast<const uint32_t*>(&pb);
+        }
+      l = l * alpha + (((s8[0] + s8[1]) + (s8[2] + s8[3])) + ((s8[4] + s8[5]) + (s8[6] + s8[7])));
+      // a rescale of O has to wait for PV_t,j-1 (PV_t,j needs this thread's P_t,j first)
+      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.f)) {
+        if (!(ok = warp_wait(&sm.pv_done[t], (j - 1) & 1, status, kFwdWaitPV))) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(lane_addr + 2 * kKeys2 + c * 32, ov);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
+          tmem_st_32x32b_x32(lane_addr + 2 * kKeys2 + c * 32, ov);
+        }
+        tmem_st_wait();
+      }
+      tmem_st_32x32b_x32(lane_addr + buf * kKeys2, packed);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&sm.p_full[t][buf]);
+    }
+    // O is final once the last PV completes. Not a parity wait on pv_done: after the last P the
+    // barrier may still be two phases behind (PV_t,n-2 pending), where the parity of phase n - 1
+    // would read as complete.
+    if (ok && warp_wait(&sm.o_ready[t], 0, status, kFwdWaitLast)) {
+      tc_fence_after();
+      const float inv = 1.f / l;
+      __nv_bfloat16* dst = out + (static_cast<int64_t>(row0 + r) * heads + h0 + t) * kDim;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t ov[32];
+        tmem_ld_32x32b_x32(lane_addr + 2 * kKeys2 + c * 32, ov);
+        tmem_ld_wait();
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          float o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(ov[g * 8 + i]) * inv;
+          store_bf16x8(dst + c * 32 + g * 8, o);
+        }
+      }
+      lse[(static_cast<int64_t>(b) * heads + h0 + t) * seq + qi * kTile + r] = (m_used + log2f(l)) * 0.69314718055994531f;
     }
   }
   tc_fence_before();
@@ -820,11 +1080,24 @@ void set_smem(Kernel kernel, size_t bytes) {
   TDSV_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
 }
 
-void launch_fwd(const at::Tensor& q, const KvMaps& kv, int kv_heads, at::Tensor& out, at::Tensor& lse,
-                long long* trace_ptr) {
+// kv: maps with 128-key boxes (one-head-per-CTA kernel); kv64: the same sources in 64-key boxes.
+void launch_fwd(const at::Tensor& q, const KvMaps& kv, const KvMaps& kv64, int kv_heads, at::Tensor& out,
+                at::Tensor& lse, long long* trace_ptr) {
   const int64_t batch = q.size(0), seq = q.size(1);
   const int heads = static_cast<int>(q.size(2));
   const CUtensorMap mq = head_major_map(q, heads, kTile);
+  if (trace_ptr == nullptr && (heads / kv_heads) % 2 == 0) {
+    // two query heads of one GQA group per CTA; K / V maps in 64-key boxes
+    const size_t smem2 = sizeof(Fwd2Smem) + 1024;
+    static std::once_flag once2;
+    std::call_once(once2, [&] { set_smem(attn_fwd2_kernel, smem2); });
+    dim3 grid2(static_cast<unsigned>(heads / 2), static_cast<unsigned>(seq / kTile), static_cast<unsigned>(batch));
+    attn_fwd2_kernel<<<grid2, kFwdThreads, smem2, stream()>>>(
+        mq, kv64, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), lse.data_ptr<float>(), static_cast<int>(seq), heads,
+        kv_heads, kLog2e / sqrtf(static_cast<float>(kDim)), status_word_ptr());
+    TDSV_LAUNCH_CHECK();
+    return;
+  }
   const size_t smem = sizeof(FwdSmem) + 1024;
   static std::once_flag once;
   std::call_once(once, [&] { set_smem(attn_fwd_kernel, smem); });
@@ -854,8 +1127,8 @@ std::vector<at::Tensor> attn_fwd(const at::Tensor& q, const at::Tensor& k, const
   auto lse = at::empty({batch, heads, seq}, q.options().dtype(at::kFloat));
   if (batch == 0 || seq == 0) return {out, lse};
   c10::cuda::CUDAGuard guard(q.device());
-  launch_fwd(q, kv_maps({reinterpret_cast<int64_t>(k.data_ptr())}, {reinterpret_cast<int64_t>(v.data_ptr())}, batch,
-                        seq, kv_heads, 0, kTile),
+  const std::vector<int64_t> kp{reinterpret_cast<int64_t>(k.data_ptr())}, vp{reinterpret_cast<int64_t>(v.data_ptr())};
+  launch_fwd(q, kv_maps(kp, vp, batch, seq, kv_heads, 0, kTile), kv_maps(kp, vp, batch, seq, kv_heads, 0, kKeys2),
              kv_heads, out, lse, trace_ptr);
   return {out, lse};
 }
@@ -879,6 +1152,7 @@ std::vector<at::Tensor> attn_fwd_cp(const at::Tensor& q, const std::vector<int64
   if (batch == 0 || seq == 0) return {out, lse};
   c10::cuda::CUDAGuard guard(q.device());
   launch_fwd(q, kv_maps(k_ptrs, v_ptrs, batch, chunk, static_cast<int>(kv_heads), q_offset, kTile),
+             kv_maps(k_ptrs, v_ptrs, batch, chunk, static_cast<int>(kv_heads), q_offset, kKeys2),
              static_cast<int>(kv_heads), out, lse, nullptr);
   return {out, lse};
 }
