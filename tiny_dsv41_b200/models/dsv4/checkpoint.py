@@ -87,8 +87,8 @@ def load_dsv41_backbone_window(folder, *, start_layer: int = 0, num_layers: int 
                                layer_loaded: Callable | None = None, engram_weights=None,
                                engram_offload: bool = False, fp4_experts: bool = False,
                                cache_quantization: str | None = None) -> DeepSeekV41ForCausalLM:
-    """``fp4_experts`` keeps the routed experts as frozen MXFP4 codes + E8M0 scales (uint8 buffers,
-    expanded per GEMM) instead of dequantising them to ``dtype`` at load. ``cache_quantization``
+    """``fp4_experts`` keeps the routed experts as frozen MXFP4 codes + E8M0 scales (uint8 buffers
+    that the grouped GEMMs read packed) instead of dequantising them to ``dtype`` at load. ``cache_quantization``
     ("none" / "hf") overrides the checkpoint config's setting."""
     folder = Path(folder)
     if engram_offload and engram_weights is not None:

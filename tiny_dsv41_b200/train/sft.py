@@ -65,7 +65,7 @@ def parse_args(argv=None):
     p.add_argument("--engram-offload", action="store_true", help="keep DSV4 Engram rows in host memory")
     p.add_argument("--train-engram", action="store_true", help="also update Engram tables in LoRA mode (SGD)")
     p.add_argument("--fp4-experts", action="store_true",
-                   help="DSV4 LoRA: keep the frozen routed experts as MXFP4 codes, expanded per GEMM")
+                   help="DSV4 LoRA: keep the frozen routed experts as MXFP4 codes, multiplied packed")
     p.add_argument("--gradient-checkpointing", action="store_true")
     p.add_argument("--seed", type=int, default=42)
     p.add_argument("--eval-batches", type=int, default=1, help="fixed evaluation batches per data group")
