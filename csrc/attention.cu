@@ -6,9 +6,9 @@
 // contraction is a tcgen05.mma with its fp32 accumulator in tensor memory, and every mbarrier wait
 // is bounded (a timeout records a status code and the CTA drains instead of spinning forever).
 //
-// Forward, GQA groups of even size (the Qwen shapes): attn_fwd2_kernel, one CTA per (128-query
-// tile, pair of query heads of one key / value head, batch); see its own comment below.
-// Forward, other group sizes (and the traced diagnostic): one CTA per (128-query tile, head, batch), 320 threads.
+// Forward, opt-in for GQA groups of even size (TDSV_ATTN_FWD2=1): attn_fwd2_kernel, one CTA per
+// (128-query tile, pair of query heads of one key / value head, batch); see its own comment below.
+// Forward, default (and the traced diagnostic): one CTA per (128-query tile, head, batch), 320 threads.
 //   warp 0     TMA producer: Q once, then K_j / V_j tiles through a two-stage ring
 //   warp 1     MMA issuer: S_{j+1} = Q K_{j+1}^T is issued before P_j is ready, so the next score
 //              tile overlaps the softmax of this one (S is double-buffered in tensor memory)
@@ -42,6 +42,7 @@
 #include "common.cuh"
 #include "tc_util.cuh"
 
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -1086,7 +1087,12 @@ void launch_fwd(const at::Tensor& q, const KvMaps& kv, const KvMaps& kv64, int k
   const int64_t batch = q.size(0), seq = q.size(1);
   const int heads = static_cast<int>(q.size(2));
   const CUtensorMap mq = head_major_map(q, heads, kTile);
-  if (trace_ptr == nullptr && (heads / kv_heads) % 2 == 0) {
+  // The two-head kernel is opt-in (TDSV_ATTN_FWD2=1, read at every launch) while a gradient
+  // difference it shows in the tiny-Qwen end-to-end comparison is open (its outputs and lse match
+  // the fp32 reference as closely as the one-head kernel's); the one-head kernel is the default.
+  const char* opt_in = std::getenv("TDSV_ATTN_FWD2");
+  const bool two_heads = opt_in != nullptr && opt_in[0] == '1';
+  if (two_heads && trace_ptr == nullptr && (heads / kv_heads) % 2 == 0) {
     // two query heads of one GQA group per CTA; K / V maps in 64-key boxes
     const size_t smem2 = sizeof(Fwd2Smem) + 1024;
     static std::once_flag once2;

@@ -38,10 +38,12 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / b.float().norm().clamp_min(1e-12)).item()
 
 
-# even GQA groups run the two-heads-per-CTA kernel, odd groups the one-head kernel
+# the default one-head kernel, and the opt-in two-heads-per-CTA kernel (even GQA groups only)
+@pytest.mark.parametrize("two_heads", [False, True])
 @pytest.mark.parametrize("batch,seq,heads,kv_heads",
                          [(1, 128, 2, 1), (1, 512, 4, 2), (2, 384, 8, 1), (1, 256, 3, 1), (2, 640, 32, 4)])
-def test_attention_forward(batch, seq, heads, kv_heads):
+def test_attention_forward(batch, seq, heads, kv_heads, two_heads, monkeypatch):
+    monkeypatch.setenv("TDSV_ATTN_FWD2", "1" if two_heads else "0")
     q, k, v = _inputs(batch, seq, heads, kv_heads)
     out, lse = ops.ext().attn_fwd(q, k, v)
     ops.check_status("attn_fwd")
