@@ -24,7 +24,11 @@ from .model import DeepSeekV41ForCausalLM, NgramHash, build_compressed_token_map
 
 
 def _prefix_config(folder: Path, num_layers: int) -> DeepSeekV41Config:
-    full = DeepSeekV41Config.from_json(folder / "config.json")
+    return prefix_config(DeepSeekV41Config.from_json(folder / "config.json"), num_layers)
+
+
+def prefix_config(full: DeepSeekV41Config, num_layers: int) -> DeepSeekV41Config:
+    """The configuration of the first ``num_layers`` real layers of a full backbone."""
     if not 1 <= num_layers <= full.num_hidden_layers:
         raise NotImplementedError(f"a full checkpoint prefix supports one to {full.num_hidden_layers} real layers")
     values = full.to_dict()
