@@ -2,6 +2,7 @@
 candidates, reward mapping, device leases and the journal."""
 
 import json
+import math
 
 from tiny_dsv41_b200.rollout.kernelbench import (KernelCase, KernelRunner, evaluate_candidate, extract_candidate,
                                                  kernel_reward)
@@ -79,3 +80,45 @@ def test_runner_leases_and_journal(tmp_path):
     assert events[-1]["counts"] == {"queued": 0, "active": 0, "completed": 3}
     rows = [json.loads(line) for line in (tmp_path / "run" / "results.jsonl").read_text().splitlines()]
     assert sorted(r["job"] for r in rows) == ["a", "b", "c"]
+
+
+def test_feedback_episode_selects_the_last_correct_turn(tmp_path):
+    """Turn 1 answers wrongly, turn 2 sees the measured verdict of turn 1 and answers correctly; the
+    correct turn is verified once more and gives the reward."""
+    from tiny_dsv41_b200.rollout.kernelbench import run_kernel_episode
+
+    case = KernelCase("relu_linear", TASK)
+    seen = []
+
+    def policy(messages):
+        seen.append(messages)
+        code = WRONG if len(messages) == 1 else GOOD
+        return "Here is my kernel.\n```python\n" + code + "```\n"
+
+    runner = KernelRunner(tmp_path / "ep", devices=("cpu",), timeout=60, trials=2, warmup=1, iters=2)
+    try:
+        record = run_kernel_episode(case, policy, runner, "Write ModelNew for this task.", turns=2, job="ep0")
+    finally:
+        runner.close()
+    assert [t["verdict"]["status"] for t in record["turns"]] == ["incorrect", "correct"], record
+    assert record["selected_turn"] == 2 and record["verification"]["status"] == "correct"
+    # the reward is the verification's (its speedup on a shared CPU is noise, so only its form is checked)
+    speedup = record["verification"]["speedup"]
+    assert speedup and record["reward"] == max(0.0, 1.0 + min(max(math.log2(speedup), -1.0), 3.0))
+    # the second request carries the first reply and its measured verdict
+    assert len(seen[1]) == 3 and seen[1][1]["role"] == "assistant" and '"status": "incorrect"' in seen[1][2]["content"]
+    events = [json.loads(line) for line in (tmp_path / "ep" / "events.jsonl").read_text().splitlines()]
+    assert {e["job"] for e in events} == {"ep0-t1", "ep0-t2", "ep0-verify"}
+
+
+def test_feedback_episode_without_a_correct_turn_has_no_reward(tmp_path):
+    from tiny_dsv41_b200.rollout.kernelbench import run_kernel_episode
+
+    runner = KernelRunner(tmp_path / "ep", devices=("cpu",), timeout=60, trials=1, warmup=1, iters=1)
+    try:
+        record = run_kernel_episode(KernelCase("relu_linear", TASK), lambda m: "no code here", runner, "task",
+                                    turns=2)
+    finally:
+        runner.close()
+    assert record["selected_turn"] is None and record["reward"] == 0.0 and record["verification"] is None
+    assert all(not t["extracted"] for t in record["turns"])

@@ -19,7 +19,10 @@ evaluation core of that loop, built for this library:
   floor checked before each start, and a JSONL journal of queued / start / finish events plus one
   result record per job;
 * :func:`kernel_reward` maps a verdict to a training reward (0 unless correct; then the clipped
-  log2 speedup plus one), the quantity GRPO groups are built from.
+  log2 speedup plus one), the quantity GRPO groups are built from;
+* :func:`run_kernel_episode` is the multi-turn loop: the policy answers, the candidate is
+  evaluated, the measured verdict goes back as the next user turn, and the last correct candidate
+  is verified once more for the reward.
 """
 
 from __future__ import annotations
@@ -290,6 +293,11 @@ class KernelRunner:
             self.results.flush()
         return verdict
 
+    def evaluate(self, job: str, case: KernelCase, candidate: str) -> KernelVerdict:
+        """One job through the same lease, memory floor and journal as :meth:`run`."""
+        self._event(job, "queued")
+        return self._one(job, case, candidate)
+
     def run(self, jobs) -> list[KernelVerdict]:
         """``jobs``: iterable of (job id, KernelCase, candidate source). Verdicts in job order."""
         jobs = list(jobs)
@@ -302,6 +310,51 @@ class KernelRunner:
     def close(self) -> None:
         self.events.close()
         self.results.close()
+
+
+def feedback_message(verdict: KernelVerdict) -> str:
+    """The next user turn of a feedback episode: the measured verdict of the previous candidate."""
+    measured = {"status": verdict.status, "detail": verdict.detail[:2000], "max_abs_error": verdict.max_abs_error,
+                "reference_ms": verdict.reference_ms, "candidate_ms": verdict.candidate_ms,
+                "speedup": verdict.speedup}
+    return ("Your previous candidate was compiled, checked and timed. Measured result:\n" + json.dumps(measured) +
+            "\nReply with a complete improved candidate: one fenced Python block defining ModelNew with the "
+            "same constructor arguments, forward signature and output shapes as Model.")
+
+
+def run_kernel_episode(case: KernelCase, generate, runner: KernelRunner, prompt, *, turns: int = 2,
+                       job: str | None = None) -> dict:
+    """A multi-turn kernel episode (the reference's ``--turns 2`` mode of ``rollout_manager/runner.py``).
+
+    ``generate(messages) -> str`` is the policy (chat messages in, assistant text out). Each turn's
+    candidate is evaluated through ``runner``; from the second turn on, the conversation carries the
+    previous reply and its measured verdict (:func:`feedback_message`). The last correct turn is
+    selected and verified once more with a fresh evaluation, whose verdict gives the reward (0 when
+    no turn was correct). Returns the episode record: per-turn candidate digests and verdicts, the
+    selected turn, the verification verdict and the reward."""
+    if turns < 1:
+        raise ValueError("an episode needs at least one turn")
+    job = job or case.case_id
+    messages = list(prompt) if isinstance(prompt, (list, tuple)) else [{"role": "user", "content": str(prompt)}]
+    record = {"job": job, "case_id": case.case_id, "turns": [], "selected_turn": None, "verification": None,
+              "reward": 0.0}
+    selected = None
+    for index in range(turns):
+        reply = generate(list(messages))
+        candidate = extract_candidate(reply) or ""
+        verdict = runner.evaluate(f"{job}-t{index + 1}", case, candidate)
+        record["turns"].append({"turn": index + 1, "candidate_sha256": verdict.candidate_sha256,
+                                "extracted": bool(candidate), "verdict": asdict(verdict)})
+        if verdict.status == "correct":
+            selected = (index + 1, candidate)
+        if index + 1 < turns:
+            messages += [{"role": "assistant", "content": reply}, {"role": "user", "content": feedback_message(verdict)}]
+    if selected is not None:
+        record["selected_turn"] = selected[0]
+        final = runner.evaluate(f"{job}-verify", case, selected[1])
+        record["verification"] = asdict(final)
+        record["reward"] = kernel_reward(final)
+    return record
 
 
 def load_cases(directory) -> list[KernelCase]:
@@ -342,4 +395,4 @@ if __name__ == "__main__":
 
 
 __all__ = ["KernelCase", "KernelRunner", "KernelVerdict", "evaluate_candidate", "extract_candidate",
-           "kernel_reward", "load_cases"]
+           "feedback_message", "kernel_reward", "load_cases", "run_kernel_episode"]
