@@ -122,3 +122,27 @@ def test_feedback_episode_without_a_correct_turn_has_no_reward(tmp_path):
         runner.close()
     assert record["selected_turn"] is None and record["reward"] == 0.0 and record["verification"] is None
     assert all(not t["extracted"] for t in record["turns"])
+
+
+NOISY = TASK.replace("return torch.relu(self.proj(x))", "return torch.relu(self.proj(x)) + torch.rand_like(x)")
+
+
+def test_reference_qualification_excludes_irreproducible_tasks(tmp_path):
+    from tiny_dsv41_b200.rollout.kernelbench import check_qualification, qualify_cases
+
+    cases = [KernelCase("stable", TASK), KernelCase("noisy", NOISY)]
+    runner = KernelRunner(tmp_path / "q", devices=("cpu",), timeout=60, trials=2, warmup=1, iters=1)
+    try:
+        catalog = qualify_cases(cases, runner)
+    finally:
+        runner.close()
+    assert catalog["tasks"]["stable"]["score_eligible"] is True
+    assert catalog["tasks"]["noisy"]["score_eligible"] is False and "incorrect" in catalog["tasks"]["noisy"]["reason"]
+    assert check_qualification(json.loads(json.dumps(catalog)), cases) == {"stable": True, "noisy": False}
+    edited = [KernelCase("stable", TASK + "\n# edited\n"), cases[1]]
+    try:
+        check_qualification(catalog, edited)
+    except ValueError:
+        pass
+    else:
+        raise AssertionError("a catalog of other task sources was accepted")

@@ -357,6 +357,53 @@ def run_kernel_episode(case: KernelCase, generate, runner: KernelRunner, prompt,
     return record
 
 
+QUALIFICATION_FORMAT = "kernel-reference-qualification-v1"
+
+
+def self_candidate(case: KernelCase) -> str:
+    """The task's own reference as a candidate (``ModelNew`` is ``Model``)."""
+    return case.source + "\n\nclass ModelNew(Model):\n    pass\n"
+
+
+def _cases_digest(cases) -> str:
+    return _sha(json.dumps(sorted((c.case_id, _sha(c.source)) for c in cases)))
+
+
+def qualify_cases(cases, runner: KernelRunner, *, job_prefix: str = "qualify") -> dict:
+    """Score eligibility of each task, decided by running its reference through the same harness as
+    a candidate (the role of the reference's ``reference_qualification.py``): a task whose reference
+    does not pass against itself (it errors, times out, or its outputs are not reproducible within
+    the task's tolerance, e.g. randomness inside ``forward``) can never be scored fairly and is
+    excluded. The catalog binds each decision to the task source digest."""
+    cases = list(cases)
+    verdicts = runner.run([(f"{job_prefix}-{c.case_id}", c, self_candidate(c)) for c in cases])
+    tasks = {}
+    for case, verdict in zip(cases, verdicts):
+        eligible = verdict.status == "correct"
+        reason = None if eligible else f"reference against itself: {verdict.status}: {verdict.detail[:300]}"
+        tasks[case.case_id] = {"source_sha256": _sha(case.source), "score_eligible": eligible, "reason": reason,
+                               "max_abs_error": verdict.max_abs_error}
+    return {"format": QUALIFICATION_FORMAT, "cases_sha256": _cases_digest(cases), "tasks": tasks}
+
+
+def check_qualification(catalog: dict, cases) -> dict[str, bool]:
+    """Eligibility per case id from a catalog of :func:`qualify_cases`, refusing one made for other
+    task sources or another set of tasks."""
+    cases = list(cases)
+    if catalog.get("format") != QUALIFICATION_FORMAT or catalog.get("cases_sha256") != _cases_digest(cases):
+        raise ValueError("the qualification catalog was made for another set of tasks")
+    tasks = catalog["tasks"]
+    if set(tasks) != {c.case_id for c in cases}:
+        raise ValueError("the qualification catalog covers other tasks")
+    out = {}
+    for case in cases:
+        item = tasks[case.case_id]
+        if item["source_sha256"] != _sha(case.source) or type(item["score_eligible"]) is not bool:
+            raise ValueError(f"qualification of {case.case_id} does not match its source")
+        out[case.case_id] = item["score_eligible"]
+    return out
+
+
 def load_cases(directory) -> list[KernelCase]:
     """Every ``*.py`` file of a directory as a case named after the file (sorted)."""
     return [KernelCase(p.stem, p.read_text(encoding="utf-8")) for p in sorted(Path(directory).glob("*.py"))]
@@ -395,4 +442,5 @@ if __name__ == "__main__":
 
 
 __all__ = ["KernelCase", "KernelRunner", "KernelVerdict", "evaluate_candidate", "extract_candidate",
-           "feedback_message", "kernel_reward", "load_cases", "run_kernel_episode"]
+           "check_qualification", "feedback_message", "kernel_reward", "load_cases", "qualify_cases",
+           "run_kernel_episode", "self_candidate"]
