@@ -4,8 +4,8 @@ candidates, reward mapping, device leases and the journal."""
 import json
 import math
 
-from tiny_dsv41_b200.rollout.kernelbench import (KernelCase, KernelRunner, evaluate_candidate, extract_candidate,
-                                                 kernel_reward)
+from tiny_dsv41_b200.rollout.kernelbench import (KernelCase, KernelRunner, KernelVerdict, evaluate_candidate,
+                                                 extract_candidate, kernel_reward)
 
 TASK = '''
 import torch
@@ -54,7 +54,11 @@ def test_verdicts_and_rewards():
     case = KernelCase("relu_linear", TASK)
     good = evaluate_candidate(case, GOOD, iters=3, warmup=1, timeout=60)
     assert good.status == "correct" and good.max_abs_error < 1e-4 and good.speedup > 0, good
-    assert kernel_reward(good) > 0
+    # a correct candidate's reward follows its measured speedup (CPU timings of a shared host are
+    # noise, so the value itself is not asserted)
+    assert kernel_reward(good) == max(0.0, 1.0 + min(max(math.log2(good.speedup), -1.0), 3.0))
+    fast = KernelVerdict("relu_linear", "x", "correct", speedup=2.0)
+    assert kernel_reward(fast) == 2.0 and kernel_reward(KernelVerdict("relu_linear", "x", "correct", speedup=64.0)) == 4.0
     wrong = evaluate_candidate(case, WRONG, iters=3, warmup=1, timeout=60)
     assert wrong.status == "incorrect" and kernel_reward(wrong) == 0.0, wrong
     broken = evaluate_candidate(case, BROKEN, timeout=60)
