@@ -45,6 +45,9 @@ def parse_args(argv=None):
     p.add_argument("--intermediate", type=int, default=768)
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--reference-experts", choices=("dsv4", "qwen"), default="dsv4",
+                   help="reference expert arm: the DeepSeek-V4 RoutedExperts (torch._grouped_mm, fused SwiGLU "
+                        "kernel, its own dispatcher) or the Qwen per-expert loop")
     p.add_argument("--kernel-breakdown", default=None, metavar="PREFIX",
                    help="write per-kernel device time of one extra untimed iteration of each arm to "
                         "PREFIX.{exchange,layer}.rankR.json (torch profiler)")
@@ -104,6 +107,26 @@ def _native_step(args, mesh, tensors, experts):
     return step
 
 
+def _reference_dsv4_experts(args, mesh, w1, w2, device):
+    """The reference's DeepSeek-V4 routed experts on its own dispatcher: dispatch, grouped GEMMs on
+    ``torch._grouped_mm``, its SwiGLU x route-weight kernel, combine. The config object carries only
+    the fields the module reads; the SwiGLU clamp is set beyond any activation (the benchmark's
+    experts are plain SwiGLU)."""
+    from types import SimpleNamespace
+
+    from dsv41_train.models.dsv4.moe.dispatch import AllToAllTokenDispatcher as Dsv4Dispatcher
+    from dsv41_train.models.dsv4.moe.module import RoutedExperts
+
+    cfg = SimpleNamespace(n_routed_experts=args.experts, hidden_size=args.hidden,
+                          moe_intermediate_size=args.intermediate, swiglu_limit=1.0e30)
+    module = RoutedExperts(cfg, Dsv4Dispatcher(mesh)).to(device=device, dtype=torch.bfloat16)
+    e = module.num_experts
+    with torch.no_grad():  # same expert weights as the other arms: [E, 2I, H] gate rows then up rows
+        module.gate_up.copy_(w1.view(e, 2, args.intermediate, args.hidden).transpose(1, 2))
+        module.down.copy_(w2)
+    return module
+
+
 def _reference_step(args, mesh, tensors, experts):
     sys.path.append(os.path.join(ROOT, "baseline", "_ref"))
     from dsv41_train.dispatch import AllToAllTokenDispatcher
@@ -113,7 +136,9 @@ def _reference_step(args, mesh, tensors, experts):
     disp = AllToAllTokenDispatcher(mesh)
     x, weights, ids, dout, w1, w2 = tensors
     module = None
-    if experts:
+    if experts and getattr(args, "reference_experts", "dsv4") == "dsv4":
+        module = _reference_dsv4_experts(args, mesh, w1, w2, x.device)
+    elif experts:
         cfg = Qwen3MoeConfig(hidden_size=args.hidden, moe_intermediate_size=args.intermediate,
                              num_experts=args.experts, num_experts_per_tok=args.topk)
         module = Qwen3MoeExperts(cfg, disp).to(x.device)
